@@ -1,0 +1,244 @@
+// C-ABI entry points of libgdn2 (declared in include/gdn2.h).
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/gdn2.h"
+#include "gdn2_kernels.cuh"
+
+using namespace gdn2;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+// Optional per-launch timing: when enabled, every kernel launch is bracketed by
+// CUDA events recorded on its own stream; gdn2_profile_read() resolves them.
+struct Profiler {
+  bool on = false;
+  struct Rec { int stage; cudaEvent_t a, b; };
+  std::vector<Rec> recs;
+  cudaEvent_t pending[kNumStages] = {};
+  double total_ms[kNumStages] = {};
+  long count[kNumStages] = {};
+};
+Profiler g_prof;
+std::mutex g_prof_mu;
+
+void prof_hook(int stage, int end, cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof.on) return;
+  cudaEvent_t ev;
+  if (cudaEventCreate(&ev) != cudaSuccess) return;
+  cudaEventRecord(ev, s);
+  if (!end) {
+    g_prof.pending[stage] = ev;
+  } else if (g_prof.pending[stage]) {
+    g_prof.recs.push_back({stage, g_prof.pending[stage], ev});
+    g_prof.pending[stage] = nullptr;
+  } else {
+    cudaEventDestroy(ev);
+  }
+}
+
+LaunchHook hook() {
+  LaunchHook h;
+  h.fn = prof_hook;
+  return h;
+}
+
+int fail(int code, const char* fmt, const char* a = "", long x = 0, long y = 0) {
+  snprintf(g_err, sizeof(g_err), fmt, a, x, y);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  snprintf(g_err, sizeof(g_err), "%s: %s", where, cudaGetErrorString(e));
+  return GDN2_ERR_CUDA;
+}
+
+int validate(int dtype, int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
+  if (dtype != GDN2_F32 && dtype != GDN2_BF16)
+    return fail(GDN2_ERR_INVALID, "unsupported dtype code %s%ld", "", dtype);
+  if (B <= 0 || T <= 0 || H <= 0)
+    return fail(GDN2_ERR_INVALID, "%sempty problem B*T*H (T=%ld, H=%ld)", "", T, H);
+  if (D != 64 && D != 128)
+    return fail(GDN2_ERR_INVALID, "%shead dim D=%ld unsupported (64 or 128)", "", D);
+  if (BT != 64 && BT != 128)
+    return fail(GDN2_ERR_INVALID, "%schunk BT=%ld unsupported (64 or 128)", "", BT);
+  if (T % BT != 0)
+    return fail(GDN2_ERR_INVALID, "%sT=%ld must be divisible by BT=%ld", "", T, BT);
+  if (BC <= 0 || BT % BC != 0)
+    return fail(GDN2_ERR_INVALID, "%ssub-block BC=%ld must divide BT=%ld", "", BC, BT);
+  if (!(clip > 0.f)) return fail(GDN2_ERR_INVALID, "%sclip must be positive");
+  if (scale != scale) return fail(GDN2_ERR_INVALID, "%sscale is NaN");
+  return GDN2_OK;
+}
+
+template <typename T>
+int run_fwd_intra(int BT, int D, const void* q, const void* k, const void* v, const void* w,
+                  const void* b, const void* g, const Problem& p, const Workspace& ws,
+                  cudaStream_t s) {
+  auto c = [](const void* x) { return static_cast<const T*>(x); };
+  cudaError_t e;
+  hook().begin(kStageFwdIntra, s);
+#define GDN2_CASE(CC, DD)                                                                  \
+  if (BT == CC && D == DD)                                                                  \
+    e = launch_fwd_intra<T, CC, DD>(c(q), c(k), c(v), c(w), c(b), c(g), p, ws, s);          \
+  else
+  GDN2_FOR_SHAPES(GDN2_CASE) return fail(GDN2_ERR_INVALID, "%sno kernel for this shape");
+#undef GDN2_CASE
+  hook().end(kStageFwdIntra, s);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "fwd_intra");
+}
+
+int run_fwd_state(int BT, int D, const Problem& p, const Workspace& ws, const float* h0, float* o,
+                  float* hf, int save, cudaStream_t s) {
+  cudaError_t e;
+  hook().begin(kStageFwdState, s);
+#define GDN2_CASE(CC, DD)                                                                  \
+  if (BT == CC && D == DD) e = launch_fwd_state<CC, DD>(p, ws, h0, o, hf, save, s); else
+  GDN2_FOR_SHAPES(GDN2_CASE) return fail(GDN2_ERR_INVALID, "%sno kernel for this shape");
+#undef GDN2_CASE
+  hook().end(kStageFwdState, s);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "fwd_state");
+}
+
+int run_bwd_state(int BT, int D, const Problem& p, const Workspace& ws, const float* dout,
+                  const float* dhf, float* dh0, cudaStream_t s) {
+  cudaError_t e;
+  hook().begin(kStageBwdState, s);
+#define GDN2_CASE(CC, DD)                                                                  \
+  if (BT == CC && D == DD) e = launch_bwd_state<CC, DD>(p, ws, dout, dhf, dh0, s); else
+  GDN2_FOR_SHAPES(GDN2_CASE) return fail(GDN2_ERR_INVALID, "%sno kernel for this shape");
+#undef GDN2_CASE
+  hook().end(kStageBwdState, s);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "bwd_state");
+}
+
+template <typename T>
+int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, const void* w,
+                  const void* b, const void* g, const float* dout, const float* dhf, void* dq,
+                  void* dk, void* dv, void* dw, void* db, void* dg, const Problem& p,
+                  const Workspace& ws, cudaStream_t s) {
+  auto c = [](const void* x) { return static_cast<const T*>(x); };
+  auto m = [](void* x) { return static_cast<T*>(x); };
+  cudaError_t e;
+#define GDN2_CASE(CC, DD)                                                                  \
+  if (BT == CC && D == DD)                                                                  \
+    e = launch_bwd_intra<T, CC, DD>(c(q), c(k), c(v), c(w), c(b), c(g), dout, dhf, m(dq),   \
+                                    m(dk), m(dv), m(dw), m(db), m(dg), p, ws, s, hook());   \
+  else
+  GDN2_FOR_SHAPES(GDN2_CASE) return fail(GDN2_ERR_INVALID, "%sno kernel for this shape");
+#undef GDN2_CASE
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "bwd_intra");
+}
+
+Problem make_problem(int B, int T, int H, int D, int BT, float scale, float clip) {
+  Problem p;
+  p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT;
+  p.scale = scale; p.clip = clip;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }
+
+int gdn2_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof.on = on != 0;
+  return GDN2_OK;
+}
+
+int gdn2_profile_read(int n, double* total_ms, long* launches, int reset) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof.recs) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      g_prof.total_ms[r.stage] += ms;
+      g_prof.count[r.stage] += 1;
+    }
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  g_prof.recs.clear();
+  for (int i = 0; i < n && i < kNumStages; ++i) {
+    if (total_ms) total_ms[i] = g_prof.total_ms[i];
+    if (launches) launches[i] = g_prof.count[i];
+  }
+  if (reset)
+    for (int i = 0; i < kNumStages; ++i) { g_prof.total_ms[i] = 0; g_prof.count[i] = 0; }
+  return kNumStages;
+}
+
+const char* gdn2_last_error(void) { return g_err; }
+
+size_t gdn2_workspace_bytes(int B, int T, int H, int D, int BT, int with_backward) {
+  if (B <= 0 || T <= 0 || H <= 0 || D <= 0 || BT <= 0 || T % BT) return 0;
+  return Workspace::required_bytes(B, H, T / BT, BT, D, with_backward != 0);
+}
+
+int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void* w,
+             const void* b, const void* g, const float* h0, float* o, float* h_final,
+             void* workspace, size_t workspace_bytes, int save_residuals, int B, int T, int H,
+             int D, int BT, int BC, float scale, float clip, void* stream) {
+  int rc = validate(dtype, B, T, H, D, BT, BC, scale, clip);
+  if (rc) return rc;
+  if (!q || !k || !v || !w || !b || !g || !o || !h_final || !workspace)
+    return fail(GDN2_ERR_INVALID, "%snull buffer pointer");
+  const size_t need = gdn2_workspace_bytes(B, T, H, D, BT, 0);
+  if (workspace_bytes < need)
+    return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
+                (long)need, (long)workspace_bytes);
+  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, false);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = dtype == GDN2_F32
+           ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
+           : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
+  if (rc) return rc;
+  return run_fwd_state(BT, D, p, ws, h0, o, h_final, save_residuals, s);
+}
+
+int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void* w,
+             const void* b, const void* g, const float* h0, const float* dout,
+             const float* dh_final, void* dq, void* dk, void* dv, void* dw, void* db, void* dg,
+             float* dh0, void* workspace, size_t workspace_bytes, int residuals_valid, int B,
+             int T, int H, int D, int BT, int BC, float scale, float clip, void* stream) {
+  int rc = validate(dtype, B, T, H, D, BT, BC, scale, clip);
+  if (rc) return rc;
+  if (!q || !k || !v || !w || !b || !g || !dout || !dh_final || !dq || !dk || !dv || !dw || !db || !dg ||
+      !dh0 || !workspace)
+    return fail(GDN2_ERR_INVALID, "%snull buffer pointer");
+  const size_t need = gdn2_workspace_bytes(B, T, H, D, BT, 1);
+  if (workspace_bytes < need)
+    return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
+                (long)need, (long)workspace_bytes);
+  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, true);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!residuals_valid) {
+    // The reference's custom_vjp keeps only the inputs and recomputes the
+    // forward in the backward (gdn2_pipeline.py:64-83); o is not needed.
+    rc = dtype == GDN2_F32
+             ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
+             : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
+    if (rc) return rc;
+    rc = run_fwd_state(BT, D, p, ws, h0, nullptr, nullptr, 1, s);
+    if (rc) return rc;
+  }
+  rc = run_bwd_state(BT, D, p, ws, dout, dh_final, dh0, s);
+  if (rc) return rc;
+  return dtype == GDN2_F32
+             ? run_bwd_intra<float>(BT, D, q, k, v, w, b, g, dout, dh_final, dq, dk, dv, dw,
+                                    db, dg, p, ws, s)
+             : run_bwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, dout, dh_final, dq, dk,
+                                            dv, dw, db, dg, p, ws, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,139 @@
+// Kernel-side declarations and the device building blocks shared by the
+// forward and backward translation units.
+#pragma once
+#include "gdn2_common.cuh"
+#include "gdn2_ws.cuh"
+
+namespace gdn2 {
+
+// Supported (chunk, head-dim) shapes.
+#define GDN2_FOR_SHAPES(X) X(64, 64) X(64, 128) X(128, 64) X(128, 128)
+#define GDN2_FOR_SHAPES_T(X)                                                                 \
+  X(float, 64, 64) X(float, 64, 128) X(float, 128, 64) X(float, 128, 128)                  \
+  X(__nv_bfloat16, 64, 64) X(__nv_bfloat16, 64, 128) X(__nv_bfloat16, 128, 64)             \
+  X(__nv_bfloat16, 128, 128)
+
+template <int W>
+__device__ __forceinline__ void store_vec(float* p, const float* v) {
+  if constexpr (W % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < W; i += 4)
+      *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < W; i += 2) *reinterpret_cast<float2*>(p + i) = make_float2(v[i], v[i + 1]);
+  }
+}
+
+template <int C, int D> struct FwdSmem {
+  static constexpr int P = C > D ? C : D;
+  static constexpr int BIG = P * (P + 4);
+  static size_t bytes() { return (size_t)(C * D + 2 * BIG + 256 + 8) * sizeof(float); }
+};
+template <int C, int D, int NV> struct StateSmem {
+  static constexpr int P = C > D ? C : D;
+  static constexpr int BIG = P * (P + 4);
+  static size_t bytes() { return (size_t)(BIG + D * NV + 2 * C * NV) * sizeof(float); }
+};
+
+// In-place (I + T)^-1 for a strictly lower-triangular C x C matrix held
+// transposed in shared memory: on entry S[j*ld + i] = T(i, j), on exit
+// S[j*ld + i] = A(i, j).  16 x 16 diagonal blocks are inverted by row-wise
+// forward substitution (gdn2_fwd.py:174-189), then blocks are composed by
+// doubling, A10 = -A11 (T10 A00), the recurrence of gdn2_fwd.py:202-211 and
+// 235-238, sanitising each product as the reference does.
+// `tmp` needs C*C/4 floats.
+template <int C>
+__device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, float clip) {
+  constexpr int MBK = 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < C / MBK && lane < MBK) {
+    const int o = warp * MBK, jj = lane;
+    float x[MBK];
+#pragma unroll
+    for (int r = 0; r < MBK; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int t = 0; t < r; ++t) s = fmaf(S[(o + t) * ld + o + r], x[t], s);
+      x[r] = (r < jj) ? 0.f : (r == jj ? san(1.f - s, clip) : san(-s, clip));
+    }
+    __syncwarp(0x0000ffffu);
+#pragma unroll
+    for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int s = 2 * MBK; s <= C; s *= 2) {
+    const int half = s / 2, per = half * half, total = (C / s) * per;
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
+      const int o = beta * s;
+      float acc = 0.f;
+      for (int kk = j; kk < half; ++kk)
+        acc = fmaf(S[(o + kk) * ld + o + half + i], S[(o + j) * ld + o + kk], acc);
+      tmp[beta * per + j * half + i] = san(acc, clip);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
+      const int o = beta * s;
+      float acc = 0.f;
+      for (int kk = 0; kk <= i; ++kk)
+        acc = fmaf(S[(o + half + kk) * ld + o + half + i], tmp[beta * per + j * half + kk], acc);
+      S[(o + j) * ld + o + half + i] = san(-acc, clip);
+    }
+    __syncthreads();
+  }
+}
+
+// Reverse (suffix) column sum of a C x D tile in shared memory (ld = D),
+// the in-chunk reverse cumsum of gdn2_bwd.py:32-41.  `tot` >= 256 floats.
+template <int C, int D>
+__device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
+  constexpr int NSEG = kThreads / D;
+  constexpr int RS = C / NSEG;
+  const int d = threadIdx.x % D, seg = threadIdx.x / D;
+  float acc = 0.f;
+  for (int r = seg * RS; r < (seg + 1) * RS; ++r) acc += s[r * D + d];
+  tot[seg * D + d] = acc;
+  __syncthreads();
+  float off = 0.f;
+  for (int sg = seg + 1; sg < NSEG; ++sg) off += tot[sg * D + d];
+  for (int r = (seg + 1) * RS - 1; r >= seg * RS; --r) {
+    off += s[r * D + d];
+    s[r * D + d] = off;
+  }
+  __syncthreads();
+}
+
+// Stage ids for the optional per-launch CUDA-event profiler of the C ABI.
+enum Stage {
+  kStageFwdIntra = 0, kStageFwdState, kStageBwdState, kStageBwdIntra1, kStageBwdIntra2,
+  kStageBwdIntra3, kNumStages
+};
+
+// Called around every kernel launch of a multi-kernel launcher (no-op unless
+// the C ABI's profiler is on).
+struct LaunchHook {
+  void (*fn)(int stage, int end, cudaStream_t s) = nullptr;
+  void begin(int st, cudaStream_t s) const { if (fn) fn(st, 0, s); }
+  void end(int st, cudaStream_t s) const { if (fn) fn(st, 1, s); }
+};
+
+// Launchers (defined in gdn2_fwd.cu / gdn2_bwd.cu).
+template <typename T, int C, int D>
+cudaError_t launch_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
+                             const T* g, const Problem& p, const Workspace& ws, cudaStream_t s);
+template <int C, int D>
+cudaError_t launch_fwd_state(const Problem& p, const Workspace& ws, const float* h0, float* o,
+                             float* hfinal, int save, cudaStream_t s);
+template <int C, int D>
+cudaError_t launch_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
+                             const float* dh_final, float* dh0, cudaStream_t s);
+template <typename T, int C, int D>
+cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
+                             const T* g, const float* dout, const float* dh_final, T* dq, T* dk,
+                             T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
+                             cudaStream_t s, const LaunchHook& hook);
+
+}  // namespace gdn2

@@ -1,0 +1,86 @@
+// Workspace layout shared by the forward and backward kernels.
+//
+// Every per-chunk tile is stored contiguously at offset
+// chunk_id * tile_elems, chunk_id = (b*H + h)*nc + c, in float32.  Tiles are
+// stored in the orientation their consumer streams into shared memory.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gdn2 {
+
+struct Problem {
+  int B, T, H, D, C, nc;   // C = chunk length BT, nc = T / C
+  float scale, clip;
+  __host__ __device__ long row_stride() const { return (long)H * D; }
+};
+
+// Float offsets (per chunk multiples) of every workspace array.
+struct Workspace {
+  float* base;
+  // forward intermediates
+  float* AqkT;   // [C][C]  Aqk transposed: element (i,j) at j*C + i
+  float* AT;     // [C][C]  A = (I+Akk)^-1 transposed
+  float* WT;     // [D][C]  W transposed
+  float* U;      // [C][D]
+  float* kg;     // [C][D]
+  float* qgT;    // [D][C]
+  float* gc;     // [C][D]  in-chunk cumulative log decay
+  float* gcl;    // [D]     sanitised gc of the last row
+  // forward residuals kept for the backward
+  float* hpre;   // [D][D]  state entering each chunk
+  float* vnew;   // [C][D]
+  // backward intermediates
+  float* dv;     // [C][D]  dv_new from the reverse state pass
+  float* dh;     // [D][D]  dh_pre of each chunk (dh_all)
+  float* dAqkT;  // [C][C]
+  float* dAkkT;  // [C][C]
+  float* dWp;    // [C][D]
+  float* pdq;    // [C][D]  partial dq  (B3)
+  float* pdk;    // [C][D]  partial dk  (B3, then B4 scratch)
+  float* pdb;    // [C][D]  partial db  (B3)
+  float* pdgc;   // [C][D]  partial dgc (B3)
+  size_t bytes;
+
+  static size_t per_chunk_floats(int C, int D, bool bwd) {
+    size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + D;   // forward
+    f += (size_t)D * D + (size_t)C * D;                        // residuals
+    if (bwd) f += 2 * (size_t)C * C + 6 * (size_t)C * D + (size_t)D * D;
+    return f;
+  }
+  static size_t required_bytes(int B, int H, int nc, int C, int D, bool bwd) {
+    return per_chunk_floats(C, D, bwd) * (size_t)B * H * nc * sizeof(float) + 256;
+  }
+  static Workspace carve(void* p, int B, int H, int nc, int C, int D, bool bwd) {
+    Workspace w{};
+    size_t n = (size_t)B * H * nc;
+    float* f = reinterpret_cast<float*>(((uintptr_t)p + 255) & ~(uintptr_t)255);
+    w.base = f;
+    auto take = [&](size_t per) { float* r = f; f += per * n; return r; };
+    w.AqkT = take((size_t)C * C);
+    w.AT = take((size_t)C * C);
+    w.WT = take((size_t)C * D);
+    w.U = take((size_t)C * D);
+    w.kg = take((size_t)C * D);
+    w.qgT = take((size_t)C * D);
+    w.gc = take((size_t)C * D);
+    w.gcl = take((size_t)D);
+    w.hpre = take((size_t)D * D);
+    w.vnew = take((size_t)C * D);
+    if (bwd) {
+      w.dv = take((size_t)C * D);
+      w.dh = take((size_t)D * D);
+      w.dAqkT = take((size_t)C * C);
+      w.dAkkT = take((size_t)C * C);
+      w.dWp = take((size_t)C * D);
+      w.pdq = take((size_t)C * D);
+      w.pdk = take((size_t)C * D);
+      w.pdb = take((size_t)C * D);
+      w.pdgc = take((size_t)C * D);
+    }
+    w.bytes = required_bytes(B, H, nc, C, D, bwd);
+    return w;
+  }
+};
+
+}  // namespace gdn2

@@ -1,0 +1,82 @@
+"""ctypes binding of libgdn2.so, the C ABI declared in include/gdn2.h.
+
+The shared library is built in-tree (``gdn2-jax-kernel_b200/build.py``) and
+loaded from this directory.  There is no fallback: if the library or a CUDA
+device is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgdn2.so")
+
+F32, BF16 = 0, 1
+OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA = 0, -1, -2, -3
+ABI_VERSION = 1
+
+_lib = None
+
+_vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+
+SIGNATURES = {
+    "gdn2_abi_version": (_i, []),
+    "gdn2_last_error": (ctypes.c_char_p, []),
+    "gdn2_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "gdn2_fwd": (_i, [_i] + [_vp] * 6 + [_vp, _vp, _vp, _vp, _sz, _i] + [_i] * 6 + [_f, _f, _vp]),
+    "gdn2_bwd": (_i, [_i] + [_vp] * 6 + [_vp, _vp, _vp] + [_vp] * 6 + [_vp, _vp, _sz, _i]
+                 + [_i] * 6 + [_f, _f, _vp]),
+    "gdn2_profile_enable": (_i, [_i]),
+    "gdn2_profile_read": (_i, [_i, ctypes.POINTER(ctypes.c_double),
+                               ctypes.POINTER(ctypes.c_long), _i]),
+}
+
+STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3")
+
+
+def profile_enable(on=True):
+    load().gdn2_profile_enable(int(on))
+
+
+def profile_read(reset=True):
+    """{stage: (total_ms, launches)} of the launches timed since the last reset."""
+    n = len(STAGES)
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_long * n)()
+    load().gdn2_profile_read(n, ms, cnt, int(reset))
+    return {s: (ms[i], cnt[i]) for i, s in enumerate(STAGES)}
+
+
+class Gdn2Error(RuntimeError):
+    """A CUDA-side failure reported by libgdn2."""
+
+
+def load():
+    """Load (once) and return the ctypes handle of libgdn2.so."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"libgdn2.so not found at {LIB_PATH}; build it with "
+            "`python gdn2-jax-kernel_b200/build.py` (nvcc, sm_100a)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.gdn2_abi_version() != ABI_VERSION:
+        raise ImportError("libgdn2.so ABI version mismatch; rebuild it")
+    _lib = lib
+    return lib
+
+
+def check(rc, what):
+    if rc == OK:
+        return
+    msg = load().gdn2_last_error().decode(errors="replace")
+    if rc == ERR_INVALID:
+        from .gdn2_fwd import Gdn2ShapeError
+        raise Gdn2ShapeError(f"{what}: {msg}")
+    raise Gdn2Error(f"{what} failed ({rc}): {msg}")

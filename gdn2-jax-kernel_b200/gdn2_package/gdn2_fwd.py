@@ -1,0 +1,187 @@
+"""GDN-2 chunked forward on B200 (mirrors the reference module gdn2_fwd.py).
+
+Public surface kept from the reference (Akseleu-J/gdn2-jax-kernel):
+  * module constants ``BT``, ``BC``, ``MB``, ``CLIP`` (gdn2_fwd.py:29-33), read
+    at call time, so ``gdn2_fwd.BT = 128`` takes effect for every later call
+    of this package (forward and backward alike);
+  * ``gdn2_pallas_forward(q,k,v,w,b,g,scale,h0=None,debug_tag="")`` returning
+    ``(o, h_final)`` (gdn2_fwd.py:400-424);
+  * ``gdn2_pallas_forward_with_residuals`` (gdn2_fwd.py:427-457).
+
+Arrays are torch tensors (B, T, H, D) in float32 or bfloat16.  CUDA tensors
+are computed in place on the current stream; CPU tensors are copied to the
+current CUDA device and the results copied back (the host-buffer path).
+``o`` and ``h_final`` are float32, as in the reference (gdn2_fwd.py:164-165).
+The compute runs in libgdn2.so (hand-written sm_100a kernels); there is no
+other backend.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+
+# ---------- constants (gdn2_fwd.py:29-33) ----------
+BT = 256     # chunk length
+BC = 128     # sub-block length (the reference's clip granularity; results do not depend on it)
+MB = 16      # micro-block of the triangular solve
+CLIP = 1e4   # stage sanitiser bound
+
+_GDN2_FWD_DIAG = os.environ.get("GDN2_FWD_DIAG", "0") == "1"
+_KERNEL_CHUNKS = (128, 64)
+_SUPPORTED_D = (64, 128)
+
+
+class Gdn2ShapeError(ValueError, AssertionError):
+    """Unsupported shape or argument.  Derives from AssertionError too, since
+    the reference rejects these with ``assert`` (gdn2_fwd.py:145-146)."""
+
+
+def _kernel_chunk(T, bt):
+    """Chunk length the kernels run with for the user's BT.  The chunked form
+    is exact for any chunk length (only the +-20 pair-decay clip and CLIP see
+    the chunking), so a BT of 256 runs as chunks of 128 when T allows it."""
+    if T % bt != 0:
+        raise Gdn2ShapeError(f"L={T} must be divisible by BT={bt}.")
+    for c in _KERNEL_CHUNKS:
+        if bt % c == 0 and T % c == 0 and c <= bt:
+            return c
+    raise Gdn2ShapeError(f"BT={bt} unsupported: kernels run chunks of 128 or 64")
+
+
+def _stage_diag(tag, x):
+    """Non-finite / large-value report when GDN2_FWD_DIAG=1 (gdn2_fwd.py:47-76)."""
+    if not _GDN2_FWD_DIAG:
+        return x
+    finite = torch.isfinite(x)
+    n_bad = int((~finite).sum())
+    mx = float(torch.where(finite, x, torch.zeros_like(x)).abs().max()) if x.numel() else 0.0
+    if n_bad:
+        print(f"[GDN2-FWD-DIAG] non-finite at {tag}: n_nonfinite={n_bad} max_abs={mx:.3e}")
+    elif mx > 1e6:
+        print(f"[GDN2-FWD-DIAG] large value at {tag}: max_abs={mx:.3e}")
+    return x
+
+
+class _Prepared:
+    """Validated, device-resident, contiguous operands of one call."""
+
+    def __init__(self, q, k, v, w, b, g, scale, h0):
+        ts = (q, k, v, w, b, g)
+        if not all(isinstance(t, torch.Tensor) for t in ts):
+            ts = tuple(torch.as_tensor(t) for t in ts)
+        shape = tuple(ts[0].shape)
+        if len(shape) != 4:
+            raise Gdn2ShapeError(f"inputs must be (B, T, H, D); got {shape}")
+        for t in ts:
+            if tuple(t.shape) != shape:
+                raise Gdn2ShapeError(f"all inputs must share shape {shape}; got {tuple(t.shape)}")
+        B, T, H, D = shape
+        if D not in _SUPPORTED_D:
+            raise Gdn2ShapeError(f"head dim D={D} unsupported (64 or 128)")
+        self.B, self.T, self.H, self.D = B, T, H, D
+        self.bt_user = int(BT)
+        self.C = _kernel_chunk(T, self.bt_user)
+        bc = int(BC)
+        if bc <= 0 or self.bt_user % bc != 0:
+            raise Gdn2ShapeError(f"BC={bc} must divide BT={self.bt_user}")
+        self.bc = bc if self.C % bc == 0 else self.C
+        if any(not t.dtype.is_floating_point for t in ts):
+            raise Gdn2ShapeError("inputs must be floating point")
+        if h0 is not None and tuple(torch.as_tensor(h0).shape) != (B, H, D, D):
+            raise Gdn2ShapeError(f"h0 must be {(B, H, D, D)}; got {tuple(torch.as_tensor(h0).shape)}")
+        self.on_host = ts[0].device.type != "cuda"
+        dev = torch.device("cuda", torch.cuda.current_device()) if self.on_host else ts[0].device
+        cdt = torch.float32 if any(t.dtype == torch.float32 or t.dtype == torch.float64 for t in ts) \
+            else torch.bfloat16
+        self.in_dtypes = tuple(t.dtype for t in ts)
+        self.dev = dev
+        self.dtype = cdt
+        self.code = _lib.F32 if cdt == torch.float32 else _lib.BF16
+        self.t = tuple(t.to(device=dev, dtype=cdt, non_blocking=True).contiguous() for t in ts)
+        self.clip = float(CLIP)
+        self.scale = float(scale)
+        if h0 is None:
+            self.h0 = None
+            self.h0_dtype = torch.float32
+        else:
+            h0 = torch.as_tensor(h0)
+            self.h0_dtype = h0.dtype
+            self.h0 = h0.to(device=dev, dtype=torch.float32, non_blocking=True).contiguous()
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def ptrs(self):
+        return [t.data_ptr() for t in self.t]
+
+    def workspace(self, with_backward):
+        n = _lib.load().gdn2_workspace_bytes(self.B, self.T, self.H, self.D, self.C,
+                                             int(with_backward))
+        if n == 0:
+            raise Gdn2ShapeError("invalid sizes for the workspace")
+        return torch.empty(n, dtype=torch.uint8, device=self.dev)
+
+
+def _run_forward(p, save_residuals=False, ws=None):
+    lib = _lib.load()
+    o = torch.empty((p.B, p.T, p.H, p.D), dtype=torch.float32, device=p.dev)
+    h_final = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
+    if ws is None:
+        ws = p.workspace(save_residuals)
+    rc = lib.gdn2_fwd(p.code, *p.ptrs(), p.h0.data_ptr() if p.h0 is not None else None,
+                      o.data_ptr(), h_final.data_ptr(), ws.data_ptr(), ws.numel(),
+                      int(save_residuals), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip,
+                      p.stream)
+    _lib.check(rc, "gdn2_fwd")
+    return o, h_final, ws
+
+
+def gdn2_pallas_forward(q, k, v, w, b, g, scale, h0=None, debug_tag=""):
+    """Full forward: Kernels A -> B -> C -> D.  Returns o (B,T,H,D) float32
+    and h_final (B,H,D,D) float32 (gdn2_fwd.py:400-424)."""
+    p = _Prepared(q, k, v, w, b, g, scale, h0)
+    o, h_final, _ = _run_forward(p)
+    o = _stage_diag(f"{debug_tag}:kernel_D_o", o)
+    h_final = _stage_diag(f"{debug_tag}:kernel_D_h_final", h_final)
+    if p.on_host:
+        return o.cpu(), h_final.cpu()
+    return o, h_final
+
+
+def _unpack_residuals(p, ws):
+    """Views of the residual tiles a forward left in `ws`, in the reference's
+    (B, H, nc, ...) layouts (see csrc/gdn2_ws.cuh for the offsets)."""
+    B, H, D, C = p.B, p.H, p.D, p.C
+    nc = p.T // C
+    n = B * H * nc
+    base = (ws.data_ptr() + 255) // 256 * 256 - ws.data_ptr()
+    f = ws[base:].view(torch.float32)
+    sizes = [("AqkT", C * C), ("AT", C * C), ("WT", C * D), ("U", C * D), ("kg", C * D),
+             ("qgT", C * D), ("gc", C * D), ("gcl", D), ("hpre", D * D), ("vnew", C * D)]
+    out, o = {}, 0
+    for name, per in sizes:
+        out[name] = f[o:o + per * n]
+        o += per * n
+    sh = lambda x, *s: x.view(B, H, nc, *s)
+    return dict(
+        Aqk=sh(out["AqkT"], C, C).transpose(-1, -2),
+        A=sh(out["AT"], C, C).transpose(-1, -2),
+        w_pseudo=sh(out["WT"], D, C).transpose(-1, -2),
+        u=sh(out["U"], C, D), kg=sh(out["kg"], C, D),
+        qg=sh(out["qgT"], D, C).transpose(-1, -2),
+        gc=sh(out["gc"], C, D), gc_last=sh(out["gcl"], D),
+        h_pre_all=sh(out["hpre"], D, D), v_new_all=sh(out["vnew"], C, D))
+
+
+def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_tag=""):
+    """Forward that also returns the per-chunk intermediates (gdn2_fwd.py:427-457):
+    Aqk, A, w_pseudo, u, kg, qg, gc_last, h_pre_all, v_new_all, all float32 in
+    the batch-major (B, H, nc, ...) layout the backward consumes.  The
+    reference additionally returns Akk, which the fused kernels never store."""
+    p = _Prepared(q, k, v, w, b, g, scale, h0)
+    o, h_final, ws = _run_forward(p, save_residuals=True)
+    res = {n: t.clone() for n, t in _unpack_residuals(p, ws).items()}
+    if p.on_host:
+        return o.cpu(), h_final.cpu(), {n: t.cpu() for n, t in res.items()}
+    return o, h_final, res

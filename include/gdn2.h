@@ -1,0 +1,81 @@
+/* libgdn2 — C ABI of the B200 (sm_100a) Gated DeltaNet-2 chunked kernels.
+ *
+ * Plain pointers and sizes only; every device buffer is owned by the caller
+ * (the library never allocates or synchronises).  All entry points are
+ * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream) and
+ * return 0 on success or a negative GDN2_ERR_* code; gdn2_last_error() then
+ * holds a one-line message for the calling thread.
+ *
+ * Tensor conventions (the reference's, Akseleu-J/gdn2-jax-kernel):
+ *   q, k, v, w, b, g        (B, T, H, D) row-major, dtype GDN2_F32 or GDN2_BF16
+ *   h0, h_final             (B, H, D, D) float32, row index = key dim
+ *   o                       (B, T, H, D) float32          (gdn2_fwd.py:164-165)
+ *   dout                    (B, T, H, D) float32 cotangent of o
+ *   dh_final                (B, H, D, D) float32 cotangent of h_final
+ *   dq, dk, dv, dw, db, dg  (B, T, H, D) in the input dtype (gdn2_pipeline.py:129-134)
+ *   dh0                     (B, H, D, D) float32
+ * BT is the chunk length (64 or 128), BC the reference's sub-block (any
+ * divisor of BT; results do not depend on it), D the head dim (64 or 128),
+ * clip the stage sanitiser bound CLIP (gdn2_fwd.py:33, 42-44).
+ */
+#ifndef GDN2_H_
+#define GDN2_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN2_ABI_VERSION 1
+
+enum { GDN2_F32 = 0, GDN2_BF16 = 1 };
+enum {
+  GDN2_OK = 0,
+  GDN2_ERR_INVALID = -1,   /* bad shape / argument (reference: AssertionError, gdn2_fwd.py:145-146) */
+  GDN2_ERR_WORKSPACE = -2, /* workspace smaller than gdn2_workspace_bytes() */
+  GDN2_ERR_CUDA = -3       /* a CUDA launch failed */
+};
+
+int gdn2_abi_version(void);
+const char* gdn2_last_error(void);
+
+/* Bytes of scratch the caller must provide.  with_backward = 0 sizes a plain
+ * forward; with_backward = 1 sizes a forward that keeps residuals plus the
+ * backward (one buffer serves both calls).  Returns 0 for invalid sizes. */
+size_t gdn2_workspace_bytes(int B, int T, int H, int D, int BT, int with_backward);
+
+/* Forward: replaces gdn2_pallas_forward(q,k,v,w,b,g,scale,h0) -> (o, h_final)
+ * (gdn2_fwd.py:400-424; Kernels A-D at gdn2_fwd.py:142, 246, 298, 338).
+ * h0 may be NULL (zero state, gdn2_fwd.py:403-404).  With save_residuals = 1
+ * the per-chunk state and v_new stay in `workspace` (which must then be sized
+ * with with_backward = 1) so gdn2_bwd can skip the forward recompute. */
+int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void* w,
+             const void* b, const void* g, const float* h0, float* o, float* h_final,
+             void* workspace, size_t workspace_bytes, int save_residuals, int B, int T, int H,
+             int D, int BT, int BC, float scale, float clip, void* stream);
+
+/* Backward of the custom_vjp: replaces _gdn2_core_bwd (gdn2_pipeline.py:70-137;
+ * B1-B5 at gdn2_bwd.py:32, 45, 99, 213, 342).  residuals_valid = 0 recomputes
+ * the forward from the inputs exactly as the reference does; 1 reuses the
+ * residuals a gdn2_fwd(save_residuals=1) call left in the same workspace.
+ * h0 may be NULL; dh_final must be given (zeros for no cotangent). */
+int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void* w,
+             const void* b, const void* g, const float* h0, const float* dout,
+             const float* dh_final, void* dq, void* dk, void* dv, void* dw, void* db, void* dg,
+             float* dh0, void* workspace, size_t workspace_bytes, int residuals_valid, int B,
+             int T, int H, int D, int BT, int BC, float scale, float clip, void* stream);
+
+/* Per-launch device timing (test and benchmark support; no counterpart in the
+ * reference).  When enabled, every kernel launch of gdn2_fwd / gdn2_bwd is
+ * bracketed by CUDA events on its stream.  gdn2_profile_read() waits for the
+ * recorded events and fills, per stage, the accumulated milliseconds and the
+ * launch count (stages: 0 fwd_intra, 1 fwd_state, 2 bwd_state, 3 bwd_intra1,
+ * 4 bwd_intra2, 5 bwd_intra3); it returns the number of stages. */
+int gdn2_profile_enable(int on);
+int gdn2_profile_read(int n, double* total_ms, long* launches, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN2_H_ */

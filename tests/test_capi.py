@@ -1,0 +1,76 @@
+"""The C ABI (include/gdn2.h) on a machine without a GPU: the library loads,
+exports every declared entry point, sizes workspaces, and rejects bad
+arguments before touching the device (the reference raises AssertionError
+for these, gdn2_fwd.py:145-146)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from gdn2_package import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "gdn2.h")).read()
+    return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(gdn2_\w+)\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared()
+    assert {"gdn2_fwd", "gdn2_bwd", "gdn2_workspace_bytes"} <= set(names)
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, n
+    assert lib.gdn2_abi_version() == _lib.ABI_VERSION
+
+
+def test_workspace_bytes():
+    lib = _lib.load()
+    B, T, H, D, C = 8, 8192, 6, 128, 128
+    nc = T // C
+    fwd = (2 * C * C + 5 * C * D + D + D * D + C * D) * 4 * B * H * nc + 256
+    bwd = fwd + (2 * C * C + 6 * C * D + D * D) * 4 * B * H * nc
+    assert lib.gdn2_workspace_bytes(B, T, H, D, C, 0) == fwd
+    assert lib.gdn2_workspace_bytes(B, T, H, D, C, 1) == bwd
+    assert lib.gdn2_workspace_bytes(B, 100, H, D, C, 0) == 0
+
+
+def _fwd(**kw):
+    a = dict(dtype=0, B=1, T=128, H=1, D=64, BT=64, BC=16, scale=0.125, clip=1e4, ws=1 << 30)
+    a.update(kw)
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(16)
+    rc = lib.gdn2_fwd(a["dtype"], *[dummy] * 6, None, dummy, dummy, dummy, a["ws"], 0,
+                      a["B"], a["T"], a["H"], a["D"], a["BT"], a["BC"], a["scale"], a["clip"], None)
+    return rc, lib.gdn2_last_error().decode()
+
+
+@pytest.mark.parametrize("kw,frag", [
+    (dict(D=96), "head dim"), (dict(BT=32), "chunk BT"), (dict(T=100), "divisible"),
+    (dict(BC=48), "sub-block"), (dict(dtype=7), "dtype"), (dict(clip=0.0), "clip"),
+    (dict(B=0), "empty"),
+])
+def test_invalid_arguments_rejected(kw, frag):
+    rc, msg = _fwd(**kw)
+    assert rc == _lib.ERR_INVALID and frag in msg
+
+
+def test_small_workspace_rejected():
+    rc, msg = _fwd(ws=1024)
+    assert rc == _lib.ERR_WORKSPACE and "workspace too small" in msg
+
+
+def test_python_api_shape_errors_match_reference_assertions():
+    import torch
+    from gdn2_package import gdn2_fwd, gdn2_pallas_forward
+    x = torch.zeros(1, 100, 2, 64)
+    with pytest.raises(AssertionError, match="divisible"):
+        gdn2_pallas_forward(x, x, x, x, x, x, 0.1)
+    gdn2_fwd.BT = 64
+    y = torch.zeros(1, 128, 2, 96)
+    with pytest.raises(ValueError, match="head dim"):
+        gdn2_pallas_forward(y, y, y, y, y, y, 0.1)
