@@ -120,7 +120,7 @@ k_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* __re
   float* X1 = sm;
   float* X2 = X1 + BIG;
   float* X3 = X2 + BIG;
-  float* colsum = X3 + BIG;   // [D]
+  float* colpart = X3 + BIG;  // [C/TM][D] per-row-group column partials
   const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
   const long rs = p.row_stride();
   const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
@@ -132,7 +132,6 @@ k_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* __re
   float *pdq = ws.pdq + chunk * C * D, *pdk = ws.pdk + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
 
-  for (int d = threadIdx.x; d < D; d += kThreads) colsum[d] = 0.f;
   load_tile_T<float>(X1, LDC, dout + off, rs, C, D);                // X1[v][i] = do(i,v)
   load_tile_T<float>(X2, LDD, hpre, D, D, D);                       // X2[v][dk] = hpre(dk,v)
   load_tile_T<float>(X3, LDC, ws.dv + chunk * C * D, D, C, D);      // X3[v][i] = dv(i,v)
@@ -213,16 +212,17 @@ k_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* __re
       store_vec<TD::TN_>(pdk + i * D + t.c0, ok);
       store_vec<TD::TN_>(pdgc + i * D + t.c0, og);
     }
-#pragma unroll
-    for (int jj = 0; jj < TD::TN_; ++jj) atomicAdd(colsum + t.c0 + jj, cs[jj]);
+    store_vec<TD::TN_>(colpart + (t.r0 / TD::TM_) * D + t.c0, cs);
   }
   __syncthreads();
   // gc_last row: sum_i dkg*kg + e^{gc_last} * sum_v dh_next * h_pre (gdn2_bwd.py:185, 196-201)
   for (int d = threadIdx.x; d < D; d += kThreads) {
     float s = 0.f;
     for (int vv = 0; vv < D; ++vv) s = fmaf(dhn[d * D + vv], hpre[d * D + vv], s);
+    float cs = 0.f;
+    for (int r = 0; r < C / TD::TM_; ++r) cs += colpart[r * D + d];   // fixed order
     const float gl = gc[(C - 1) * D + d];
-    pdgc[(C - 1) * D + d] += colsum[d] + __expf(gl) * s;
+    pdgc[(C - 1) * D + d] += cs + __expf(gl) * s;
   }
 }
 
@@ -588,7 +588,8 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
   cudaError_t e;
   {
     hook.begin(kStageBwdIntra1, s);
-    const size_t smem = (size_t)(3 * BIG + D) * sizeof(float);
+    using TD = typename TileFor<C, D>::type;
+    const size_t smem = (size_t)(3 * BIG + (C / TD::TM_) * D) * sizeof(float);
     auto kern = k_bwd_intra1<T, C, D>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
