@@ -1,0 +1,198 @@
+// Blackwell (sm_100a) tensor-core building blocks: tcgen05.mma kind::tf32
+// with TMEM accumulators, used as 3xTF32 (a = hi + lo; D += hi*hi + hi*lo +
+// lo*hi) for float32-accurate products.
+//
+// Shared-memory operand layout ("canonical tile"): an R x K float tile is a
+// grid of core matrices of 8 rows x 16 bytes (4 floats), stored row-group
+// major with the 4-column chunks fastest:
+//   byte(r, c) = ((r/8) * (K/4) + c/4) * 128 + (r%8) * 16 + (c%4) * 4.
+// The same storage serves as a K-major operand (contraction over the columns)
+// or, through the descriptor's major bit, as an MN-major operand (contraction
+// over the rows); no-swizzle layout, 16-byte aligned.
+//
+// Every wait on an mbarrier is bounded; on expiry the kernel records an error
+// code in a caller-provided device status word and proceeds.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn2 {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t canon_off(int r, int c, int K) {
+  return (uint32_t)((((r >> 3) * (K >> 2)) + (c >> 2)) * 128 + (r & 7) * 16 + (c & 3) * 4);
+}
+
+// Split x into a tf32-exact head (low 13 mantissa bits cleared) and the rest.
+__device__ __forceinline__ void split(float x, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  lo = x - hi;
+}
+__device__ __forceinline__ void split4(float4 v, float4& h, float4& l) {
+  split(v.x, h.x, l.x); split(v.y, h.y, l.y); split(v.z, h.z, l.z); split(v.w, h.w, l.w);
+}
+
+// Store 4 consecutive columns (c % 4 == 0) of row r of an R x K canonical tile
+// pair (hi plane, lo plane).
+__device__ __forceinline__ void st_split4(float* hi, float* lo, int r, int c, int K, float4 v) {
+  float4 h, l;
+  split4(v, h, l);
+  const uint32_t o = canon_off(r, c, K) >> 2;
+  *reinterpret_cast<float4*>(hi + o) = h;
+  *reinterpret_cast<float4*>(lo + o) = l;
+}
+
+// --------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor (no swizzle): start >> 4 at [0,14),
+// leading byte offset >> 4 at [16,30), stride byte offset >> 4 at [32,46),
+// descriptor version 1 at [46,48), layout type 0 (none) at [61,64).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3fff) | ((uint64_t)((lbo >> 4) & 0x3fff) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
+}
+
+// Operand view of a canonical tile for a K-slice walk.
+//   K-major  (tile rows = M/N, cols = K):  LBO = 128, SBO = (cols/4)*128,
+//            one k-step (8 columns) advances 256 bytes.
+//   MN-major (tile rows = K, cols = M/N):  SBO = 128, LBO = (cols/4)*128,
+//            one k-step (8 rows) advances (cols/4)*128 bytes.
+struct Opnd {
+  uint32_t hi, lo;      // shared addresses of the two planes
+  uint32_t lbo, sbo, step;
+  uint32_t mn_major;
+};
+__device__ __forceinline__ Opnd kmajor(const float* hi, const float* lo, int cols) {
+  return Opnd{smem_u32(hi), smem_u32(lo), 128u, (uint32_t)(cols / 4) * 128u, 256u, 0u};
+}
+__device__ __forceinline__ Opnd mnmajor(const float* hi, const float* lo, int cols) {
+  const uint32_t cb = (uint32_t)(cols / 4) * 128u;
+  return Opnd{smem_u32(hi), smem_u32(lo), cb, 128u, cb, 1u};
+}
+__device__ __forceinline__ Opnd advance(Opnd o, int ksteps) {
+  o.hi += o.step * ksteps;
+  o.lo += o.step * ksteps;
+  return o;
+}
+
+// Instruction descriptor, kind::tf32, f32 accumulate: c_format F32 (1) at
+// [4,6), a/b format TF32 (2) at [7,10) / [10,13), a/b major at bits 15/16,
+// N >> 3 at [17,23), M >> 4 at [24,29).
+__device__ __forceinline__ uint32_t idesc_tf32(int M, int N, uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (a_mn << 15) | (b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// D[128 x N] (+)= A[128 x 8*ksteps] * B[N x 8*ksteps]^T in 3xTF32.  Issued by
+// one thread.  `accumulate` = 0 overwrites D on the first product.
+__device__ __forceinline__ void mma3(uint32_t d_tmem, const Opnd& A, const Opnd& B, int N,
+                                     int ksteps, uint32_t accumulate) {
+  const uint32_t id = idesc_tf32(128, N, A.mn_major, B.mn_major);
+  for (int s = 0; s < ksteps; ++s) {
+    const uint64_t ah = sdesc(A.hi + s * A.step, A.lbo, A.sbo);
+    const uint64_t al = sdesc(A.lo + s * A.step, A.lbo, A.sbo);
+    const uint64_t bh = sdesc(B.hi + s * B.step, B.lbo, B.sbo);
+    const uint64_t bl = sdesc(B.lo + s * B.step, B.lbo, B.sbo);
+    mma_tf32(d_tmem, al, bh, id, (s > 0 || accumulate) ? 1u : 0u);
+    mma_tf32(d_tmem, ah, bl, id, 1u);
+    mma_tf32(d_tmem, ah, bh, id, 1u);
+  }
+}
+
+// ------------------------------------------------------------------ barriers
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Status word written on a timed-out wait (a device int the caller provides).
+constexpr int kErrWaitTimeout = 1;
+constexpr long long kWaitLimit = 1ll << 22;
+
+// Wait for the phase with parity `parity` of `bar` to complete; bounded.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t a = smem_u32(bar);
+  for (long long it = 0; it < kWaitLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  if (err) atomicExch(err, kErrWaitTimeout);
+  return false;
+}
+
+// Arrive on `bar` when every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// -------------------------------------------------------------------- TMEM
+// Allocate `ncols` (power of two >= 32) TMEM columns; called by one full warp.
+// The base address is written to *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols)
+               : "memory");
+}
+
+// Load 16 consecutive f32 columns of this thread's TMEM lane.  `taddr` must
+// carry the warp's lane quarter in bits [16, 32): (32 * (warp % 4)) << 16.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t lane_quarter_addr(uint32_t tmem_base, int col) {
+  const int warp = threadIdx.x >> 5;
+  return tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)col;
+}
+
+}  // namespace tc
+}  // namespace gdn2
