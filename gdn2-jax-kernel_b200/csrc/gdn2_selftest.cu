@@ -1,7 +1,8 @@
 // Self-test of the tcgen05 3xTF32 building blocks (gdn2_tc.cuh): a batched
 // 128 x N x K float32 product through canonical shared-memory tiles and a
-// TMEM accumulator, in every operand orientation.  Exposed through the C ABI
-// so the tests can check the descriptor encodings on the GPU.
+// TMEM accumulator.  Exposed through the C ABI so the tests can check the
+// descriptor encodings on the GPU.  trans_a / trans_b stage the operand from a
+// transposed source through the register transpose the kernels use.
 #include "../../include/gdn2.h"
 #include "gdn2_common.cuh"
 #include "gdn2_tc.cuh"
@@ -9,11 +10,11 @@
 namespace gdn2 {
 
 // D[b] = A[b] (128 x K, row-major) * B[b] (K x N, row-major), float32.
-// a_mn / b_mn choose how each operand is staged: 0 = K-major canonical tile,
-// 1 = MN-major canonical tile.
+// Both operands are staged K-major; trans_a / trans_b pick gathered loads or
+// 4x4 register-transposed loads for the staging.
 __global__ void __launch_bounds__(kThreads, 1)
 k_selftest_gemm(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ D,
-                int K, int N, int a_mn, int b_mn, int* err) {
+                int K, int N, int trans_a, int trans_b, int* err) {
   constexpr int KS = 32;
   __shared__ __align__(16) float a_hi[128 * KS], a_lo[128 * KS];
   extern __shared__ __align__(16) float dyn[];   // b_hi, b_lo: N*KS each
@@ -39,27 +40,27 @@ k_selftest_gemm(const float* __restrict__ A, const float* __restrict__ B, float*
   for (int k0 = 0; k0 < K; k0 += KS) {
     // A slice: 128 rows (m) x KS cols (k)
     for (int e = tid; e < 128 * KS / 4; e += kThreads) {
-      if (!a_mn) {
-        const int m = e / (KS / 4), kk = (e % (KS / 4)) * 4;
-        tc::st_split4(a_hi, a_lo, m, kk, KS,
-                      *reinterpret_cast<const float4*>(Ab + (size_t)m * K + k0 + kk));
-      } else {   // tile rows = k, cols = m
-        const int kk = e / 32, m = (e % 32) * 4;
-        float4 v = make_float4(Ab[(size_t)m * K + k0 + kk], Ab[(size_t)(m + 1) * K + k0 + kk],
-                               Ab[(size_t)(m + 2) * K + k0 + kk], Ab[(size_t)(m + 3) * K + k0 + kk]);
-        tc::st_split4(a_hi, a_lo, kk, m, 128, v);
-      }
+      const int m = e / (KS / 4), kk = (e % (KS / 4)) * 4;
+      const float* p = Ab + (size_t)m * K + k0 + kk;
+      const float4 v = trans_a ? make_float4(p[0], p[1], p[2], p[3])
+                               : *reinterpret_cast<const float4*>(p);
+      tc::st_split4(a_hi, a_lo, m, kk, KS, v);
     }
-    for (int e = tid; e < N * KS / 4; e += kThreads) {
-      if (b_mn) {   // tile rows = k, cols = n
-        const int kk = e / (N / 4), n = (e % (N / 4)) * 4;
-        tc::st_split4(b_hi, b_lo, kk, n, N,
-                      *reinterpret_cast<const float4*>(Bb + (size_t)(k0 + kk) * N + n));
-      } else {      // tile rows = n, cols = k
+    if (!trans_b) {
+      for (int e = tid; e < N * KS / 4; e += kThreads) {   // tile rows = n, cols = k
         const int n = e / (KS / 4), kk = (e % (KS / 4)) * 4;
         float4 v = make_float4(Bb[(size_t)(k0 + kk) * N + n], Bb[(size_t)(k0 + kk + 1) * N + n],
                                Bb[(size_t)(k0 + kk + 2) * N + n], Bb[(size_t)(k0 + kk + 3) * N + n]);
         tc::st_split4(b_hi, b_lo, n, kk, KS, v);
+      }
+    } else {
+      for (int e = tid; e < (N / 4) * (KS / 4); e += kThreads) {   // 4x4 blocks
+        const int n = (e % (N / 4)) * 4, kk = (e / (N / 4)) * 4;
+        const float* p = Bb + (size_t)(k0 + kk) * N + n;
+        tc::st_split4x4T(b_hi, b_lo, n, kk, KS, *reinterpret_cast<const float4*>(p),
+                         *reinterpret_cast<const float4*>(p + N),
+                         *reinterpret_cast<const float4*>(p + 2 * N),
+                         *reinterpret_cast<const float4*>(p + 3 * N));
       }
     }
     tc::fence_async_smem();
@@ -67,8 +68,8 @@ k_selftest_gemm(const float* __restrict__ A, const float* __restrict__ B, float*
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
-      const tc::Opnd Ao = a_mn ? tc::mnmajor(a_hi, a_lo, 128) : tc::kmajor(a_hi, a_lo, KS);
-      const tc::Opnd Bo = b_mn ? tc::mnmajor(b_hi, b_lo, N) : tc::kmajor(b_hi, b_lo, KS);
+      const tc::Opnd Ao = tc::kmajor(a_hi, a_lo, KS);
+      const tc::Opnd Bo = tc::kmajor(b_hi, b_lo, KS);
       tc::mma3(tmem, Ao, Bo, N, KS / 8, k0 > 0);
       tc::commit(&bar);
     }
@@ -93,7 +94,7 @@ k_selftest_gemm(const float* __restrict__ A, const float* __restrict__ B, float*
 }  // namespace gdn2
 
 extern "C" int gdn2_selftest_gemm_tf32x3(const float* A, const float* B, float* D, int batch,
-                                         int K, int N, int a_mn, int b_mn, int* status,
+                                         int K, int N, int trans_a, int trans_b, int* status,
                                          void* stream) {
   if (batch <= 0 || K <= 0 || K % 32 || N < 32 || N > 256 || N % 32) return GDN2_ERR_INVALID;
   const size_t smem = (size_t)2 * N * 32 * sizeof(float);
@@ -101,6 +102,6 @@ extern "C" int gdn2_selftest_gemm_tf32x3(const float* A, const float* B, float* 
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return GDN2_ERR_CUDA;
   gdn2::k_selftest_gemm<<<batch, gdn2::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      A, B, D, K, N, a_mn, b_mn, status);
+      A, B, D, K, N, trans_a, trans_b, status);
   return cudaGetLastError() == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
 }

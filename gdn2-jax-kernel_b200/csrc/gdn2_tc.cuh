@@ -6,9 +6,11 @@
 // grid of core matrices of 8 rows x 16 bytes (4 floats), stored row-group
 // major with the 4-column chunks fastest:
 //   byte(r, c) = ((r/8) * (K/4) + c/4) * 128 + (r%8) * 16 + (c%4) * 4.
-// The same storage serves as a K-major operand (contraction over the columns)
-// or, through the descriptor's major bit, as an MN-major operand (contraction
-// over the rows); no-swizzle layout, 16-byte aligned.
+// Operands are always K-major: the contraction index runs along the columns
+// of the stored tile (no-swizzle layout, 16-byte aligned).  Measured on B200
+// (tests/test_gpu_tc.py): an MN-major (transposed) kind::tf32 operand yields
+// an all-zero product, so a transposed operand is transposed while it is
+// staged instead.
 //
 // Every wait on an mbarrier is bounded; on expiry the kernel records an error
 // code in a caller-provided device status word and proceeds.
@@ -46,6 +48,17 @@ __device__ __forceinline__ void st_split4(float* hi, float* lo, int r, int c, in
   *reinterpret_cast<float4*>(lo + o) = l;
 }
 
+// Rows r0..r0+3 of a 4x4 block given as 4 float4 rows of the transposed
+// source (src row j = tile column c + j, columns = tile rows r0..r0+3):
+// transpose in registers and store 4 tile rows of 4 columns each.
+__device__ __forceinline__ void st_split4x4T(float* hi, float* lo, int r0, int c, int K, float4 s0,
+                                             float4 s1, float4 s2, float4 s3) {
+  st_split4(hi, lo, r0 + 0, c, K, make_float4(s0.x, s1.x, s2.x, s3.x));
+  st_split4(hi, lo, r0 + 1, c, K, make_float4(s0.y, s1.y, s2.y, s3.y));
+  st_split4(hi, lo, r0 + 2, c, K, make_float4(s0.z, s1.z, s2.z, s3.z));
+  st_split4(hi, lo, r0 + 3, c, K, make_float4(s0.w, s1.w, s2.w, s3.w));
+}
+
 // --------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (no swizzle): start >> 4 at [0,14),
 // leading byte offset >> 4 at [16,30), stride byte offset >> 4 at [32,46),
@@ -55,11 +68,9 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
          ((uint64_t)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
 }
 
-// Operand view of a canonical tile for a K-slice walk.
-//   K-major  (tile rows = M/N, cols = K):  LBO = 128, SBO = (cols/4)*128,
-//            one k-step (8 columns) advances 256 bytes.
-//   MN-major (tile rows = K, cols = M/N):  SBO = 128, LBO = (cols/4)*128,
-//            one k-step (8 rows) advances (cols/4)*128 bytes.
+// K-major operand view of a canonical tile (rows = M or N, cols = K):
+// LBO = 128 (the two 16-byte K chunks of one k-step), SBO = (cols/4)*128
+// (between 8-row groups); one k-step (8 columns) advances 256 bytes.
 struct Opnd {
   uint32_t hi, lo;      // shared addresses of the two planes
   uint32_t lbo, sbo, step;
@@ -67,10 +78,6 @@ struct Opnd {
 };
 __device__ __forceinline__ Opnd kmajor(const float* hi, const float* lo, int cols) {
   return Opnd{smem_u32(hi), smem_u32(lo), 128u, (uint32_t)(cols / 4) * 128u, 256u, 0u};
-}
-__device__ __forceinline__ Opnd mnmajor(const float* hi, const float* lo, int cols) {
-  const uint32_t cb = (uint32_t)(cols / 4) * 128u;
-  return Opnd{smem_u32(hi), smem_u32(lo), cb, 128u, cb, 1u};
 }
 __device__ __forceinline__ Opnd advance(Opnd o, int ksteps) {
   o.hi += o.step * ksteps;

@@ -77,12 +77,12 @@ int gdn2_profile_read(int n, double* total_ms, long* launches, int reset);
 
 /* Self-test of the tensor-core building block (no counterpart in the
  * reference): D[b] = A[b] (128 x K) * B[b] (K x N), float32 row-major device
- * arrays, computed with tcgen05 kind::tf32 in 3xTF32 form.  a_mn / b_mn pick
- * the shared-memory orientation of each operand (0 K-major, 1 MN-major).
+ * arrays, computed with tcgen05 kind::tf32 in 3xTF32 form.  trans_a / trans_b pick
+ * how each operand is staged (1 = through a 4x4 register transpose).
  * K % 32 == 0, N in {32, 64, ..., 256}.  *status (device int) receives 1 if a
  * barrier wait timed out. */
 int gdn2_selftest_gemm_tf32x3(const float* A, const float* B, float* D, int batch, int K, int N,
-                              int a_mn, int b_mn, int* status, void* stream);
+                              int trans_a, int trans_b, int* status, void* stream);
 
 #ifdef __cplusplus
 }
