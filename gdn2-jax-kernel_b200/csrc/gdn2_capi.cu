@@ -145,6 +145,15 @@ Problem make_problem(int B, int T, int H, int D, int BT, float scale, float clip
 
 }  // namespace
 
+namespace gdn2 {
+// Lets other translation units of the library report a message through
+// gdn2_last_error().
+int report_error(int code, const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+}  // namespace gdn2
+
 extern "C" {
 
 int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }

@@ -66,6 +66,22 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
              float* dh0, void* workspace, size_t workspace_bytes, int residuals_valid, int B,
              int T, int H, int D, int BT, int BC, float scale, float clip, void* stream);
 
+/* Forward for callers that cannot allocate device memory (no counterpart in
+ * the reference).  Same arguments and results as gdn2_fwd without the
+ * workspace: the scratch lives in a fixed device array of
+ * GDN2_NOALLOC_SCRATCH_BYTES inside the library, present on every GPU that
+ * loads it until the process exits.  Problems whose forward workspace
+ * (gdn2_workspace_bytes(..., 0)) exceeds that size are rejected with
+ * GDN2_ERR_WORKSPACE.  The first call on a device looks up the array's device
+ * address (make that first call before any stream capture).  All calls share
+ * the one array, so calls that overlap on the GPU (different streams or
+ * threads without ordering) race with each other. */
+#define GDN2_NOALLOC_SCRATCH_BYTES (64u << 20)
+int gdn2_fwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* w,
+                     const void* b, const void* g, const float* h0, float* o, float* h_final,
+                     int B, int T, int H, int D, int BT, int BC, float scale, float clip,
+                     void* stream);
+
 /* Per-launch device timing (test and benchmark support; no counterpart in the
  * reference).  When enabled, every kernel launch of gdn2_fwd / gdn2_bwd is
  * bracketed by CUDA events on its stream.  gdn2_profile_read() waits for the
