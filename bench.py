@@ -42,6 +42,12 @@ def flops_per_chunk(C, D):
         "bwd_intra1": 6 * C * D * D + C * C * D,         # dqg, dWp, dkg, dAqk
         "bwd_intra2": 6 * C * C * D + 4 * C ** 3 / 3,    # dA (2), dkb, dwv, dA A^T, A^T tmp
         "bwd_intra3": 4 * C * C * D,                     # four pair-sum products of B4
+        "fwd_affine": 4 * C * D * D,                     # kg^T W, kg^T U
+        "fwd_scan": 2 * D ** 3,                          # M h (serial)
+        "fwd_out": 4 * C * D * D + C * C * D,            # W h, qg h, Aqk vnew
+        "bwd_prep": 4 * C * D * D + C * C * D,           # Aqk^T do, qg^T do, W^T dvp
+        "bwd_scan": 2 * D ** 3,                          # M^T dh (serial)
+        "bwd_dvn": 2 * C * D * D,                        # kg dh_next
     }
 
 
@@ -56,6 +62,12 @@ def bytes_per_chunk(C, D):
         "bwd_intra1": 2 * t + 3 * t + 2 * s + 3 * t + cc,
         "bwd_intra2": 5 * t + 2 * cc + t + 3 * t + 2 * t + cc,
         "bwd_intra3": 4 * t + 2 * cc + 5 * t + 4 * t,
+        "fwd_affine": 3 * t + 2 * s,
+        "fwd_scan": 3 * s,
+        "fwd_out": 3 * t + s + cc + 3 * t,
+        "bwd_prep": cc + 3 * t + t + s,
+        "bwd_scan": 3 * s,
+        "bwd_dvn": 3 * t + s,
     }
 
 

@@ -136,6 +136,10 @@ int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "bwd_intra");
 }
 
+// Chunk = head dim = 128 runs the inter-chunk recurrence on the tensor cores
+// (affine scan, gdn2_tc_kernels.cu); other shapes use the CUDA-core kernels.
+bool use_tc(int BT, int D) { return BT == 128 && D == 128; }
+
 Problem make_problem(int B, int T, int H, int D, int BT, float scale, float clip) {
   Problem p;
   p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT;
@@ -211,6 +215,10 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
            ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
            : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
   if (rc) return rc;
+  if (use_tc(BT, D)) {
+    cudaError_t e = launch_tc_fwd(p, ws, h0, o, h_final, s, hook());
+    return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "tc_fwd");
+  }
   return run_fwd_state(BT, D, p, ws, h0, o, h_final, save_residuals, s);
 }
 
@@ -238,11 +246,21 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
              ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
              : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
     if (rc) return rc;
-    rc = run_fwd_state(BT, D, p, ws, h0, nullptr, nullptr, 1, s);
+    if (use_tc(BT, D)) {
+      cudaError_t e = launch_tc_fwd(p, ws, h0, nullptr, nullptr, s, hook());
+      if (e != cudaSuccess) return cuda_fail(e, "tc_fwd");
+    } else {
+      rc = run_fwd_state(BT, D, p, ws, h0, nullptr, nullptr, 1, s);
+      if (rc) return rc;
+    }
+  }
+  if (use_tc(BT, D)) {
+    cudaError_t e = launch_tc_bwd_state(p, ws, dout, dh_final, dh0, s, hook());
+    if (e != cudaSuccess) return cuda_fail(e, "tc_bwd_state");
+  } else {
+    rc = run_bwd_state(BT, D, p, ws, dout, dh_final, dh0, s);
     if (rc) return rc;
   }
-  rc = run_bwd_state(BT, D, p, ws, dout, dh_final, dh0, s);
-  if (rc) return rc;
   return dtype == GDN2_F32
              ? run_bwd_intra<float>(BT, D, q, k, v, w, b, g, dout, dh_final, dq, dk, dv, dw,
                                     db, dg, p, ws, s)

@@ -109,7 +109,8 @@ __device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
 // Stage ids for the optional per-launch CUDA-event profiler of the C ABI.
 enum Stage {
   kStageFwdIntra = 0, kStageFwdState, kStageBwdState, kStageBwdIntra1, kStageBwdIntra2,
-  kStageBwdIntra3, kNumStages
+  kStageBwdIntra3, kStageFwdAffine, kStageFwdScan, kStageFwdOut, kStageBwdPrep, kStageBwdScan,
+  kStageBwdDvn, kNumStages
 };
 
 // Called around every kernel launch of a multi-kernel launcher (no-op unless
@@ -135,5 +136,12 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,
                              T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
                              cudaStream_t s, const LaunchHook& hook);
+
+// Tensor-core path (chunk = head dim = 128, float32 workspace), gdn2_tc_kernels.cu.
+cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,
+                          float* hfinal, cudaStream_t s, const LaunchHook& hook);
+cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
+                                const float* dh_final, float* dh0, cudaStream_t s,
+                                const LaunchHook& hook);
 
 }  // namespace gdn2

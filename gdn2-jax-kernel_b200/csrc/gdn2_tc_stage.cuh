@@ -1,0 +1,123 @@
+// Staging of 128 x 32 K-slices of float32 operands from global memory into
+// canonical 3xTF32 shared-memory tiles (see gdn2_tc.cuh), with a per-element
+// transform, and the double-buffered slice loop around tcgen05.mma.
+#pragma once
+#include "gdn2_common.cuh"
+#include "gdn2_tc.cuh"
+
+namespace gdn2 {
+namespace tc {
+
+constexpr int KS = 32;                               // K-slice width
+constexpr int SLICE_FLOATS = 128 * KS;               // one plane of one slice
+constexpr int SLICE_BYTES = 2 * SLICE_FLOATS * 4;    // hi + lo planes
+
+struct Ident {
+  __device__ __forceinline__ float4 operator()(float4 v) const { return v; }
+};
+struct Scale {
+  float s;
+  __device__ __forceinline__ float4 operator()(float4 v) const {
+    return make_float4(s * v.x, s * v.y, s * v.z, s * v.w);
+  }
+};
+
+// tile(r, k) = src[r * ld + k0 + k], r < 128, k < 32.  A warp covers 8 rows x
+// 4 column chunks, so its 16-byte shared stores span all 8 bank quads.
+template <class F>
+__device__ __forceinline__ void stage_direct(float* hi, float* lo, const float* __restrict__ src,
+                                             long ld, int k0, F f) {
+#pragma unroll
+  for (int it = 0; it < 1024 / kThreads; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const int lane = e & 31, w = e >> 5;
+    const int r = (w & 15) * 8 + (lane & 7);
+    const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(src + r * ld + k0 + c);
+    st_split4(hi, lo, r, c, KS, f(v));
+  }
+}
+
+// tile(r, k) = src[(k0 + k) * ld + r]: 4 x 4 blocks read as 4 float4 rows of
+// the source and transposed in registers.  The store order of the 4 tile rows
+// is rotated by lane so a warp's stores spread over the 8 bank quads.
+template <class F>
+__device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* __restrict__ src,
+                                            long ld, int k0, F f) {
+  const int e = threadIdx.x;                       // 256 blocks of 4 x 4
+  const int rb = (e & 7) + ((e >> 5) & 3) * 8;     // 32 row blocks
+  const int kb = ((e >> 3) & 3) + (e >> 7) * 4;    // 8 column blocks
+  const int r0 = rb * 4, c0 = kb * 4;
+  const float* p = src + (long)(k0 + c0) * ld + r0;
+  const float4 s0 = *reinterpret_cast<const float4*>(p);
+  const float4 s1 = *reinterpret_cast<const float4*>(p + ld);
+  const float4 s2 = *reinterpret_cast<const float4*>(p + 2 * ld);
+  const float4 s3 = *reinterpret_cast<const float4*>(p + 3 * ld);
+  const float4 t0 = make_float4(s0.x, s1.x, s2.x, s3.x), t1 = make_float4(s0.y, s1.y, s2.y, s3.y);
+  const float4 t2 = make_float4(s0.z, s1.z, s2.z, s3.z), t3 = make_float4(s0.w, s1.w, s2.w, s3.w);
+  const int rot = (e >> 3) & 3;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int j = (t + rot) & 3;
+    const float4 v = j == 0 ? t0 : (j == 1 ? t1 : (j == 2 ? t2 : t3));
+    st_split4(hi, lo, r0 + j, c0, KS, f(v));
+  }
+}
+
+// Slice ring of two buffers, each holding NOP operand slices.
+struct Ring {
+  float* base;          // 2 * nop * SLICE_BYTES bytes
+  uint64_t* bars;       // 2 mbarriers (one per buffer)
+  uint32_t phase[2];
+  int nop;
+  __device__ __forceinline__ float* hi(int buf, int op) const {
+    return base + (size_t)(buf * nop + op) * 2 * SLICE_FLOATS;
+  }
+  __device__ __forceinline__ float* lo(int buf, int op) const { return hi(buf, op) + SLICE_FLOATS; }
+  __device__ __forceinline__ Opnd op(int buf, int o) const {
+    return kmajor(hi(buf, o), lo(buf, o), KS);
+  }
+};
+
+// Make the staged slices visible to the tensor core and to the issuing thread.
+__device__ __forceinline__ void slice_publish() {
+  fence_async_smem();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+}
+
+// Wait until the MMAs that last read buffer `buf` completed (no-op for the
+// first use of each buffer).
+__device__ __forceinline__ void ring_acquire(Ring& r, int buf, int uses, int* err) {
+  if (uses > 0) {
+    mbar_wait(&r.bars[buf], r.phase[buf], err);
+    r.phase[buf] ^= 1;
+  }
+}
+
+// Wait for every MMA issued so far (commit to `bar`, then all threads wait).
+__device__ __forceinline__ void drain(uint64_t* bar, uint32_t& phase, int* err) {
+  if (threadIdx.x == 0) commit(bar);
+  mbar_wait(bar, phase, err);
+  phase ^= 1;
+  fence_after_sync();
+}
+
+// This thread's share of a 128 x N accumulator: warp w owns lanes 32*(w%4)..
+// and the column half w/4.  fn(row, col, v[16]) for each 16 columns.
+template <int N, class Fn>
+__device__ __forceinline__ void for_acc(uint32_t tmem, int col0, Fn fn) {
+  const int warp = threadIdx.x >> 5;
+  const int row = 32 * (warp & 3) + (threadIdx.x & 31);
+  const int half = warp >> 2;
+#pragma unroll 1
+  for (int c = half * (N / 2); c < (half + 1) * (N / 2); c += 16) {
+    float v[16];
+    tmem_ld16(lane_quarter_addr(tmem, col0 + c), v);
+    fn(row, c, v);
+  }
+}
+
+}  // namespace tc
+}  // namespace gdn2

@@ -40,16 +40,23 @@ struct Workspace {
   float* pdk;    // [C][D]  partial dk  (B3, then B4 scratch)
   float* pdb;    // [C][D]  partial db  (B3)
   float* pdgc;   // [C][D]  partial dgc (B3)
+  // affine form of the state recurrence (tensor-core path)
+  float* M;      // [D][D]  diag(e^{gc_last}) - kg^T W
+  float* Bc;     // [D][D]  kg^T U
+  float* E;      // [D][D]  scale qg^T do - W^T dv_partial
+  float* dvp;    // [C][D]  dv_partial = san(Aqk^T do)
+  int* status;   // device status word (1 = a bounded wait timed out); sticky
   size_t bytes;
 
   static size_t per_chunk_floats(int C, int D, bool bwd) {
     size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + D;   // forward
     f += (size_t)D * D + (size_t)C * D;                        // residuals
-    if (bwd) f += 2 * (size_t)C * C + 6 * (size_t)C * D + (size_t)D * D;
+    f += 2 * (size_t)D * D;                                    // M, Bc
+    if (bwd) f += 2 * (size_t)C * C + 7 * (size_t)C * D + 2 * (size_t)D * D;
     return f;
   }
   static size_t required_bytes(int B, int H, int nc, int C, int D, bool bwd) {
-    return per_chunk_floats(C, D, bwd) * (size_t)B * H * nc * sizeof(float) + 256;
+    return per_chunk_floats(C, D, bwd) * (size_t)B * H * nc * sizeof(float) + 512;
   }
   static Workspace carve(void* p, int B, int H, int nc, int C, int D, bool bwd) {
     Workspace w{};
@@ -67,6 +74,8 @@ struct Workspace {
     w.gcl = take((size_t)D);
     w.hpre = take((size_t)D * D);
     w.vnew = take((size_t)C * D);
+    w.M = take((size_t)D * D);
+    w.Bc = take((size_t)D * D);
     if (bwd) {
       w.dv = take((size_t)C * D);
       w.dh = take((size_t)D * D);
@@ -77,7 +86,10 @@ struct Workspace {
       w.pdk = take((size_t)C * D);
       w.pdb = take((size_t)C * D);
       w.pdgc = take((size_t)C * D);
+      w.E = take((size_t)D * D);
+      w.dvp = take((size_t)C * D);
     }
+    w.status = reinterpret_cast<int*>(f);
     w.bytes = required_bytes(B, H, nc, C, D, bwd);
     return w;
   }

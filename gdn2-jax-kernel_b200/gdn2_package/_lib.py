@@ -34,7 +34,8 @@ SIGNATURES = {
                                ctypes.POINTER(ctypes.c_long), _i]),
 }
 
-STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3")
+STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3",
+          "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan", "bwd_dvn")
 
 
 def profile_enable(on=True):
