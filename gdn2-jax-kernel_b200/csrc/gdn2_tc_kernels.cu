@@ -156,42 +156,65 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   }
   uint32_t ph = 0;
   int g = 0;   // slice counter over the whole scan (ring phases)
+  // Register prefetch: this thread's share of the next M (4 slices) and of
+  // the constant term it adds in the epilogue (row v, 64 columns d).
+  const int warp = threadIdx.x >> 5;
+  const int vrow = 32 * (warp & 3) + (threadIdx.x & 31);
+  const int dcol0 = (warp >> 2) * 64;
+  Frag mf[4];
+  float addv[64];
+  auto load_m = [&](int c) {
+    const float* m = ws.M + (bh * p.nc + c) * D * D;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      if (!BWD) load_direct(mf[s], m, D, s * KS);
+      else load_trans(mf[s], m, D, s * KS);
+    }
+  };
+  auto load_add = [&](int c) {
+    const float* add = (BWD ? ws.E : ws.Bc) + (bh * p.nc + c) * D * D;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) addv[j] = __ldg(add + (dcol0 + j) * D + vrow);
+  };
+  load_m(BWD ? p.nc - 1 : 0);
   for (int it = 0; it < p.nc; ++it) {
     const int c = BWD ? p.nc - 1 - it : it;
     const size_t chunk = bh * p.nc + c;
-    const float* m = ws.M + chunk * D * D;
+    load_add(c);
     for (int s = 0; s < D / KS; ++s, ++g) {
       const int buf = g & 1;
       ring_acquire(ring, buf, g >> 1, ws.status);
-      if (!BWD)
-        stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), m, D, s * KS, Ident{});  // (d, d') = M
-      else
-        stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), m, D, s * KS, Ident{});   // (d', d) = M(d, d')
+      if (!BWD) store_direct(ring.hi(buf, 0), ring.lo(buf, 0), mf[s]);   // (d, d') = M
+      else store_trans(ring.hi(buf, 0), ring.lo(buf, 0), mf[s]);         // (d', d) = M(d, d')
       slice_publish();
       if (threadIdx.x == 0) {
         mma3(tmem, kmajor(s_hi(s), s_lo(s), KS), ring.op(buf, 0), 128, KS / 8, s > 0);
         commit(&ring.bars[buf]);
       }
     }
+    if (it + 1 < p.nc) load_m(BWD ? c - 1 : c + 1);
     drain(&ts.done, ph, ws.status);
-    const float* add = (BWD ? ws.E : ws.Bc) + chunk * D * D;
     const bool last = it == p.nc - 1;
     float* dst;
     if (!BWD) dst = last ? (out_final ? out_final + bh * D * D : nullptr) : ws.hpre + (chunk + 1) * D * D;
     else dst = ws.dh + chunk * D * D;
-    for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c0 = dcol0 + q * 16;
+      float x[16];
+      tmem_ld16(lane_quarter_addr(tmem, c0), x);
       float y[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        y[j] = san(x[j] + add[(c0 + j) * D + v], p.clip);
-        if (dst) dst[(c0 + j) * D + v] = y[j];
-        if (BWD && last) out_final[bh * D * D + (c0 + j) * D + v] = san(y[j], 1e4f);
+        y[j] = san(x[j] + addv[q * 16 + j], p.clip);
+        if (dst) dst[(c0 + j) * D + vrow] = y[j];
+        if (BWD && last) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y[j], 1e4f);
       }
       const int s = c0 / KS, cc = c0 % KS;
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
-        st_split4(s_hi(s), s_lo(s), v, cc + j, KS, make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]));
-    });
+        st_split4(s_hi(s), s_lo(s), vrow, cc + j, KS, make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]));
+    }
   }
   tc_teardown(tmem, 128);
 }

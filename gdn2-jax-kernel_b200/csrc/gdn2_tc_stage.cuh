@@ -64,6 +64,55 @@ __device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* _
   }
 }
 
+// Split forms of the two staging patterns: load a thread's share of a slice
+// into registers (so the load can be issued early), store it later.
+struct Frag {
+  float4 v[4];
+};
+__device__ __forceinline__ void load_direct(Frag& f, const float* __restrict__ src, long ld, int k0) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const int lane = e & 31, w = e >> 5;
+    const int r = (w & 15) * 8 + (lane & 7);
+    const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
+    f.v[it] = __ldg(reinterpret_cast<const float4*>(src + r * ld + k0 + c));
+  }
+}
+__device__ __forceinline__ void store_direct(float* hi, float* lo, const Frag& f) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const int lane = e & 31, w = e >> 5;
+    const int r = (w & 15) * 8 + (lane & 7);
+    const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
+    st_split4(hi, lo, r, c, KS, f.v[it]);
+  }
+}
+__device__ __forceinline__ void load_trans(Frag& f, const float* __restrict__ src, long ld, int k0) {
+  const int e = threadIdx.x;
+  const int rb = (e & 7) + ((e >> 5) & 3) * 8;
+  const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
+  const float* p = src + (long)(k0 + kb * 4) * ld + rb * 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f.v[j] = __ldg(reinterpret_cast<const float4*>(p + j * ld));
+}
+__device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f) {
+  const int e = threadIdx.x;
+  const int rb = (e & 7) + ((e >> 5) & 3) * 8;
+  const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
+  const int r0 = rb * 4, c0 = kb * 4;
+  const float4 s0 = f.v[0], s1 = f.v[1], s2 = f.v[2], s3 = f.v[3];
+  const float4 t0 = make_float4(s0.x, s1.x, s2.x, s3.x), t1 = make_float4(s0.y, s1.y, s2.y, s3.y);
+  const float4 t2 = make_float4(s0.z, s1.z, s2.z, s3.z), t3 = make_float4(s0.w, s1.w, s2.w, s3.w);
+  const int rot = (e >> 3) & 3;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int j = (t + rot) & 3;
+    st_split4(hi, lo, r0 + j, c0, KS, j == 0 ? t0 : (j == 1 ? t1 : (j == 2 ? t2 : t3)));
+  }
+}
+
 // Slice ring of two buffers, each holding NOP operand slices.
 struct Ring {
   float* base;          // 2 * nop * SLICE_BYTES bytes
