@@ -582,11 +582,11 @@ template <typename T, int C, int D>
 cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,
                              T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
-                             cudaStream_t s, const LaunchHook& hook) {
+                             cudaStream_t s, const LaunchHook& hook, bool skip12) {
   constexpr int P = C > D ? C : D, BIG = P * (P + 4);
   const dim3 grid(p.nc, p.H, p.B);
   cudaError_t e;
-  {
+  if (!skip12) {
     hook.begin(kStageBwdIntra1, s);
     using TD = typename TileFor<C, D>::type;
     const size_t smem = (size_t)(3 * BIG + (C / TD::TM_) * D) * sizeof(float);
@@ -597,7 +597,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     hook.end(kStageBwdIntra1, s);
   }
-  {
+  if (!skip12) {
     hook.begin(kStageBwdIntra2, s);
     const size_t smem = (size_t)(2 * BIG) * sizeof(float);
     auto kern = k_bwd_intra2<T, C, D>;
@@ -629,7 +629,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
   template cudaError_t launch_bwd_intra<T, C, D>(                                            \
       const T*, const T*, const T*, const T*, const T*, const T*, const float*, const float*, \
       T*, T*, T*, T*, T*, T*, const Problem&, const Workspace&, cudaStream_t,                \
-      const LaunchHook&);
+      const LaunchHook&, bool);
 GDN2_FOR_SHAPES(GDN2_INST_BSTATE)
 GDN2_FOR_SHAPES_T(GDN2_INST_BINTRA)
 

@@ -126,10 +126,17 @@ int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
   auto c = [](const void* x) { return static_cast<const T*>(x); };
   auto m = [](void* x) { return static_cast<T*>(x); };
   cudaError_t e;
+  const bool tc = BT == 128 && D == 128;
+  if (tc) {
+    e = launch_tc_bwd_intra12<T>(c(q), c(k), c(v), c(w), c(b), dout, dhf, m(dv), m(dw), p, ws,
+                                 s, hook());
+    if (e != cudaSuccess) return cuda_fail(e, "tc_bwd_intra");
+  }
 #define GDN2_CASE(CC, DD)                                                                  \
   if (BT == CC && D == DD)                                                                  \
     e = launch_bwd_intra<T, CC, DD>(c(q), c(k), c(v), c(w), c(b), c(g), dout, dhf, m(dq),   \
-                                    m(dk), m(dv), m(dw), m(db), m(dg), p, ws, s, hook());   \
+                                    m(dk), m(dv), m(dw), m(db), m(dg), p, ws, s, hook(),    \
+                                    tc);                                                    \
   else
   GDN2_FOR_SHAPES(GDN2_CASE) return fail(GDN2_ERR_INVALID, "%sno kernel for this shape");
 #undef GDN2_CASE

@@ -135,7 +135,12 @@ template <typename T, int C, int D>
 cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,
                              T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
-                             cudaStream_t s, const LaunchHook& hook);
+                             cudaStream_t s, const LaunchHook& hook, bool skip12 = false);
+template <typename T>
+cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w, const T* b,
+                                  const float* dout, const float* dh_final, T* dv_out, T* dw_out,
+                                  const Problem& p, const Workspace& ws, cudaStream_t s,
+                                  const LaunchHook& hook);
 
 // Tensor-core path (chunk = head dim = 128, float32 workspace), gdn2_tc_kernels.cu.
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,

@@ -113,6 +113,30 @@ __device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f)
   }
 }
 
+// Loader forms: ld(r, c) returns tile(r, c..c+3) (direct), or ld(kk, r0)
+// returns tile(r0..r0+3, kk), i.e. one float4 row of the transposed source.
+template <class L>
+__device__ __forceinline__ void stage_direct_f(float* hi, float* lo, L ld) {
+#pragma unroll
+  for (int it = 0; it < 1024 / kThreads; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const int lane = e & 31, w = e >> 5;
+    const int r = (w & 15) * 8 + (lane & 7);
+    const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
+    st_split4(hi, lo, r, c, KS, ld(r, c));
+  }
+}
+template <class L>
+__device__ __forceinline__ void stage_trans_f(float* hi, float* lo, L ld) {
+  const int e = threadIdx.x;
+  const int rb = (e & 7) + ((e >> 5) & 3) * 8;
+  const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
+  Frag f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f.v[j] = ld(kb * 4 + j, rb * 4);
+  store_trans(hi, lo, f);
+}
+
 // Slice ring of two buffers, each holding NOP operand slices.
 struct Ring {
   float* base;          // 2 * nop * SLICE_BYTES bytes
@@ -142,6 +166,22 @@ __device__ __forceinline__ void ring_acquire(Ring& r, int buf, int uses, int* er
   if (uses > 0) {
     mbar_wait(&r.bars[buf], r.phase[buf], err);
     r.phase[buf] ^= 1;
+  }
+}
+
+// One K = 128 pass in four 32-wide slices: stage(buf, s) fills the buffer,
+// issue(buf, s) (thread 0) issues the MMAs that read it.
+template <class St, class Is>
+__device__ __forceinline__ void kloop(Ring& ring, int& g, int* err, St stage, Is issue) {
+  for (int s = 0; s < 128 / KS; ++s, ++g) {
+    const int buf = g & 1;
+    ring_acquire(ring, buf, g >> 1, err);
+    stage(buf, s);
+    slice_publish();
+    if (threadIdx.x == 0) {
+      issue(buf, s);
+      commit(&ring.bars[buf]);
+    }
   }
 }
 
