@@ -15,10 +15,10 @@ constexpr int C = 128, D = 128;
 constexpr float kFinalClipTc = 1e4f;   // gdn2_pipeline.py:34
 
 struct TcSmemB {
+  float colpart[8][D];   // first member: 16-byte aligned for float4 stores
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
-  float colpart[4][D];
 };
 
 __device__ __forceinline__ uint32_t setup(TcSmemB* s) {
@@ -54,6 +54,14 @@ __device__ __forceinline__ Ring ring_of(float* base, TcSmemB* s, int nop) {
 __device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
   *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
 }
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ldg4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 san4(float4 v, float c) {
+  return make_float4(san(v.x, c), san(v.y, c), san(v.z, c), san(v.w, c));
+}
+__device__ __forceinline__ float4 exp4(float4 v) {
+  return make_float4(__expf(v.x), __expf(v.y), __expf(v.z), __expf(v.w));
+}
 
 }  // namespace
 
@@ -67,7 +75,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* __restrict__ dout,
                 const float* __restrict__ dh_final, Problem p, Workspace ws) {
   extern __shared__ __align__(128) float sm[];
-  __shared__ TcSmemB ts;
+  __shared__ __align__(16) TcSmemB ts;
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % p.nc);
   const size_t bh = chunk / p.nc;
@@ -87,92 +95,77 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   Ring ring = ring_of(sm, &ts, 3);
   int g = 0;
   // contraction over the value dim v for every product
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), doc, rs, s * KS, Ident{});      // (i,v)
-          stage_direct(ring.hi(buf, 1), ring.lo(buf, 1), dvn, D, s * KS, Scale{-1.f});    // (i,v)
-          stage_direct(ring.hi(buf, 2), ring.lo(buf, 2), hpre, D, s * KS, Ident{});      // (dk,v)
-        },
-        [&](int buf, int s) {
-          mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-          mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
-        });
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), vnew, D, s * KS, Ident{});      // (i|j,v)
-          stage_direct(ring.hi(buf, 1), ring.lo(buf, 1), doc, rs, s * KS, Ident{});      // (i,v)
-          stage_direct(ring.hi(buf, 2), ring.lo(buf, 2), dhn, D, s * KS, Ident{});       // (dk,v)
-        },
-        [&](int buf, int s) {
-          mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-          mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);
-        });
+  {
+    const Src srcs[3] = {direct(doc, rs), direct(dvn, D, -1.f), direct(hpre, D)};  // (i,v) (i,v) (dk,v)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
+    });
+  }
+  {
+    const Src srcs[3] = {direct(vnew, D), direct(doc, rs), direct(dhn, D)};  // (i|j,v) (i,v) (dk,v)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);
+    });
+  }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
-  // dqg -> pdq = san(dqg e^gc), pdgc = dqg qg
-  for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4) {
-      float oq[4], og[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int d = c0 + j + t;
-        const float eg = __expf(gc[i * D + d]);
-        const float dqg = p.scale * x[j + t];
-        oq[t] = san(dqg * eg, p.clip);
-        og[t] = dqg * (to_f<T>(qc[i * rs + d]) * eg);
-      }
-      st4(pdq + i * D + c0 + j, oq[0], oq[1], oq[2], oq[3]);
-      st4(pdgc + i * D + c0 + j, og[0], og[1], og[2], og[3]);
-    }
-  });
+  float* t0 = sm;                  // the ring is free: two padded 128 x 128 tiles
+  float* t1 = sm + TILE_FLOATS;
+  acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
+  acc_to_smem<false>(tmem, 128, t1);   // dWp
+  __syncthreads();
   float* dwp = ws.dWp + chunk * C * D;
-  for_acc<128>(tmem, 128, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4) st4(dwp + i * D + c0 + j, x[j], x[j + 1], x[j + 2], x[j + 3]);
+  for_tile([&](int i, int d) {
+    const float4 x = lds4(t0 + i * TLD + d);
+    const float4 eg = exp4(ldg4(gc + i * D + d));
+    const float4 qv = ld4<T>(qc + i * rs + d);
+    const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
+    st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
+        san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
+    st4(pdgc + i * D + d, dqg.x * (qv.x * eg.x), dqg.y * (qv.y * eg.y), dqg.z * (qv.z * eg.z),
+        dqg.w * (qv.w * eg.w));
+    *reinterpret_cast<float4*>(dwp + i * D + d) = lds4(t1 + i * TLD + d);
   });
+  __syncthreads();
+  acc_to_smem<true>(tmem, 384, t0);    // t0[j][i] = dAqk(i, j)
+  acc_to_smem<false>(tmem, 256, t1);   // dkg
+  __syncthreads();
   float* daqkT = ws.dAqkT + chunk * C * C;
-  for_acc<128>(tmem, 384, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int jj = c0 + j;
-      daqkT[jj * C + i] = (jj <= i) ? san(x[j], p.clip) : 0.f;
-    }
+  for_tile([&](int j, int i) {
+    const float4 x = lds4(t0 + j * TLD + i);
+    st4(daqkT + j * C + i, j <= i ? san(x.x, p.clip) : 0.f, j <= i + 1 ? san(x.y, p.clip) : 0.f,
+        j <= i + 2 ? san(x.z, p.clip) : 0.f, j <= i + 3 ? san(x.w, p.clip) : 0.f);
   });
   // dkg -> pdk = dkg e^{gc_last - gc}; pdgc -= dkg kg; column sums of dkg kg
   const float* gl = gc + (C - 1) * D;
-  const int warp = threadIdx.x >> 5;
-  for_acc<128>(tmem, 256, [&](int i, int c0, const float* x) {
-    float ok[16], og[16], xs[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int d = c0 + j;
-      const float f = __expf(gl[d] - gc[i * D + d]);
-      xs[j] = x[j] * (to_f<T>(kc[i * rs + d]) * f);
-      ok[j] = x[j] * f;
-      og[j] = pdgc[i * D + d] - xs[j];
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j += 4) {
-      st4(pdk + i * D + c0 + j, ok[j], ok[j + 1], ok[j + 2], ok[j + 3]);
-      st4(pdgc + i * D + c0 + j, og[j], og[j + 1], og[j + 2], og[j + 3]);
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float v = xs[j];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if ((threadIdx.x & 31) == 0) ts.colpart[warp & 3][c0 + j] = v;
-    }
+  float cs[4] = {0.f, 0.f, 0.f, 0.f};
+  for_tile([&](int i, int d) {
+    const float4 x = lds4(t1 + i * TLD + d);
+    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gl + d);
+    const float4 kv = ld4<T>(kc + i * rs + d);
+    const float4 f = exp4(make_float4(l4.x - g4.x, l4.y - g4.y, l4.z - g4.z, l4.w - g4.w));
+    const float4 xs = make_float4(x.x * (kv.x * f.x), x.y * (kv.y * f.y), x.z * (kv.z * f.z),
+                                  x.w * (kv.w * f.w));
+    st4(pdk + i * D + d, x.x * f.x, x.y * f.y, x.z * f.z, x.w * f.w);
+    const float4 pg = ldg4(pdgc + i * D + d);
+    st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
+    cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
   });
+  {
+    const int d = (threadIdx.x & 31) * 4;
+    st4(&ts.colpart[threadIdx.x >> 5][d], cs[0], cs[1], cs[2], cs[3]);
+  }
   __syncthreads();
   // gc_last row: sum_i dkg kg + e^{gc_last} sum_v dh_next h_pre (gdn2_bwd.py:185, 196-201)
   if (threadIdx.x < D) {
     const int d = threadIdx.x;
-    float s = 0.f;
-    for (int vv = 0; vv < D; ++vv) s = fmaf(dhn[d * D + vv], hpre[d * D + vv], s);
-    const float cs = ((ts.colpart[0][d] + ts.colpart[1][d]) + ts.colpart[2][d]) + ts.colpart[3][d];
-    pdgc[(C - 1) * D + d] += cs + __expf(gl[d]) * s;
+    float sdot = 0.f;
+    for (int vv = 0; vv < D; ++vv) sdot = fmaf(dhn[d * D + vv], hpre[d * D + vv], sdot);
+    float csum = 0.f;
+    for (int r = 0; r < 8; ++r) csum += ts.colpart[r][d];   // fixed order
+    pdgc[(C - 1) * D + d] += csum + __expf(gl[d]) * sdot;
   }
   teardown(tmem);
 }
@@ -189,7 +182,7 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
                 const T* __restrict__ b, T* __restrict__ dv_out, T* __restrict__ dw_out, Problem p,
                 Workspace ws) {
   extern __shared__ __align__(128) float sm[];
-  __shared__ TcSmemB ts;
+  __shared__ __align__(16) TcSmemB ts;
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % p.nc);
   const size_t bh = chunk / p.nc;
@@ -208,108 +201,105 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   int g = 0;
   uint32_t ph = 0;
   // dA = dWp kb^T + dv wv^T  (contraction over d)
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), dwp, D, s * KS, Ident{});       // (i,d)
-          stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {          // (j,d) kb
-            const int d = s * KS + cc;
-            const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
-            const float4 g4 = *reinterpret_cast<const float4*>(gc + j * D + d);
-            return make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
-                               bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
-          });
-        },
-        [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), dvn, D, s * KS, Ident{});       // (i,d)
-          stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {          // (j,d) wv
-            const int d = s * KS + cc;
-            const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
-            return make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
-          });
-        },
-        [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1); });
+  {
+    const Src srcs[1] = {direct(dwp, D)};   // (i,d)
+    kloop_pf(ring, g, ws.status, srcs,
+             [&](int buf, int s) {
+               stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) kb
+                 const int d = s * KS + cc;
+                 const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+                 const float4 g4 = *reinterpret_cast<const float4*>(gc + j * D + d);
+                 return make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
+                                    bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
+               });
+             },
+             [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
+  }
+  {
+    const Src srcs[1] = {direct(dvn, D)};   // (i,d)
+    kloop_pf(ring, g, ws.status, srcs,
+             [&](int buf, int s) {
+               stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) wv
+                 const int d = s * KS + cc;
+                 const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
+                 return make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
+               });
+             },
+             [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1); });
+  }
   drain(&ts.done, ph, ws.status);
-  for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4)
-      st4(dA + i * C + c0 + j, san(x[j], p.clip), san(x[j + 1], p.clip), san(x[j + 2], p.clip),
-          san(x[j + 3], p.clip));
+  float* t0 = sm;
+  float* t1 = sm + TILE_FLOATS;
+  acc_to_smem<false>(tmem, 0, t0);
+  __syncthreads();
+  for_tile([&](int i, int c4) {
+    *reinterpret_cast<float4*>(dA + i * C + c4) = san4(lds4(t0 + i * TLD + c4), p.clip);
   });
   __syncthreads();
   // tmp = san(dA A^T)  (contraction over k)
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), dA, C, s * KS, Ident{});       // (i,k)
-          stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), at, C, s * KS, Ident{});         // (j,k)=A(j,k)
-        },
-        [&](int buf, int s) { mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
+  {
+    const Src srcs[2] = {direct(dA, C), trans(at, C)};   // (i,k) = dA, (j,k) = A(j,k)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+    });
+  }
   drain(&ts.done, ph, ws.status);
-  for_acc<128>(tmem, 128, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4)
-      st4(tmp + i * C + c0 + j, san(x[j], p.clip), san(x[j + 1], p.clip), san(x[j + 2], p.clip),
-          san(x[j + 3], p.clip));
+  acc_to_smem<false>(tmem, 128, t0);
+  __syncthreads();
+  for_tile([&](int i, int c4) {
+    *reinterpret_cast<float4*>(tmp + i * C + c4) = san4(lds4(t0 + i * TLD + c4), p.clip);
   });
   __syncthreads();
   // dAkk = -(A^T tmp): (i, j) = sum_k A(k, i) tmp(k, j)
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), at, C, s * KS, Ident{});       // (i,k)=A(k,i)
-          stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), tmp, C, s * KS, Ident{});       // (j,k)=tmp(k,j)
-        },
-        [&](int buf, int s) { mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
+  {
+    const Src srcs[2] = {direct(at, C), trans(tmp, C)};   // (i,k) = A(k,i), (j,k) = tmp(k,j)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+    });
+  }
   // dkb = A^T dWp, dwv = A^T dv: (j, d) = sum_i A(i, j) X(i, d)
-  kloop(ring, g, ws.status,
-        [&](int buf, int s) {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), at, C, s * KS, Ident{});       // (j,i)=A(i,j)
-          stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), dwp, D, s * KS, Ident{});       // (d,i)
-          stage_trans(ring.hi(buf, 2), ring.lo(buf, 2), dvn, D, s * KS, Ident{});       // (d,i)
-        },
-        [&](int buf, int s) {
-          mma3(tmem + 384, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-          mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-        });
+  {
+    const Src srcs[3] = {direct(at, C), trans(dwp, D), trans(dvn, D)};   // (j,i) (d,i) (d,i)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem + 384, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+    });
+  }
   drain(&ts.done, ph, ws.status);
   float* dAkkT = ws.dAkkT + chunk * C * C;
-  for_acc<128>(tmem, 256, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int jj = c0 + j;
-      dAkkT[jj * C + i] = (jj < i) ? san(-x[j], p.clip) : 0.f;
-    }
+  acc_to_smem<true>(tmem, 256, t0);    // t0[j][i] = acc(i, j)
+  acc_to_smem<false>(tmem, 384, t1);   // dkb (j, d)
+  __syncthreads();
+  for_tile([&](int j, int i) {
+    const float4 x = lds4(t0 + j * TLD + i);
+    st4(dAkkT + j * C + i, j < i ? san(-x.x, p.clip) : 0.f, j < i + 1 ? san(-x.y, p.clip) : 0.f,
+        j < i + 2 ? san(-x.z, p.clip) : 0.f, j < i + 3 ? san(-x.w, p.clip) : 0.f);
   });
   float *pdk = ws.pdk + chunk * C * D, *pdb = ws.pdb + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
-  for_acc<128>(tmem, 384, [&](int j, int c0, const float* x) {
-#pragma unroll
-    for (int t = 0; t < 16; t += 4) {
-      float ok[4], ob[4], og[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int d = c0 + t + u;
-        const float eg = __expf(gc[j * D + d]);
-        const float kk = to_f<T>(kc[j * rs + d]), bv = to_f<T>(bc[j * rs + d]);
-        const float dkb = x[t + u];
-        ok[u] = san(pdk[j * D + d] + dkb * eg * bv, p.clip);
-        ob[u] = san(dkb * eg * kk, p.clip);
-        og[u] = san(pdgc[j * D + d] + dkb * (bv * kk * eg), p.clip);
-      }
-      st4(pdk + j * D + c0 + t, ok[0], ok[1], ok[2], ok[3]);
-      st4(pdb + j * D + c0 + t, ob[0], ob[1], ob[2], ob[3]);
-      st4(pdgc + j * D + c0 + t, og[0], og[1], og[2], og[3]);
-    }
+  for_tile([&](int j, int d) {
+    const float4 x = lds4(t1 + j * TLD + d);
+    const float4 eg = exp4(ldg4(gc + j * D + d));
+    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+    const float4 pk = ldg4(pdk + j * D + d), pg = ldg4(pdgc + j * D + d);
+    st4(pdk + j * D + d, san(pk.x + x.x * eg.x * bv.x, p.clip), san(pk.y + x.y * eg.y * bv.y, p.clip),
+        san(pk.z + x.z * eg.z * bv.z, p.clip), san(pk.w + x.w * eg.w * bv.w, p.clip));
+    st4(pdb + j * D + d, san(x.x * eg.x * kv.x, p.clip), san(x.y * eg.y * kv.y, p.clip),
+        san(x.z * eg.z * kv.z, p.clip), san(x.w * eg.w * kv.w, p.clip));
+    st4(pdgc + j * D + d, san(pg.x + x.x * (bv.x * kv.x * eg.x), p.clip),
+        san(pg.y + x.y * (bv.y * kv.y * eg.y), p.clip), san(pg.z + x.z * (bv.z * kv.z * eg.z), p.clip),
+        san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
   });
-  for_acc<128>(tmem, 0, [&](int j, int c0, const float* x) {
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const int d = c0 + t;
-      dw_out[off + j * rs + d] =
-          from_f<T>(san(san(x[t] * to_f<T>(vc[j * rs + d]), p.clip), kFinalClipTc));
-      dv_out[off + j * rs + d] =
-          from_f<T>(san(san(x[t] * to_f<T>(wc[j * rs + d]), p.clip), kFinalClipTc));
-    }
+  __syncthreads();
+  acc_to_smem<false>(tmem, 0, t0);     // dwv (j, d)
+  __syncthreads();
+  for_tile([&](int j, int d) {
+    const float4 x = lds4(t0 + j * TLD + d);
+    const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4<T>(wc + j * rs + d);
+    const float4 dw = make_float4(x.x * vv.x, x.y * vv.y, x.z * vv.z, x.w * vv.w);
+    const float4 dvv = make_float4(x.x * wv.x, x.y * wv.y, x.z * wv.z, x.w * wv.w);
+    st4<T>(dw_out + off + j * rs + d, san4(san4(dw, p.clip), kFinalClipTc));
+    st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
   });
   teardown(tmem);
 }

@@ -83,19 +83,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   const float* kg = ws.kg + chunk * C * D;
   const float* wt = ws.WT + chunk * C * D;
   const float* u = ws.U + chunk * C * D;
-  for (int s = 0; s < C / KS; ++s) {
-    const int buf = s & 1;
-    ring_acquire(ring, buf, s >> 1, ws.status);
-    stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), kg, D, s * KS, Ident{});   // (d, i) = kg(i, d)
-    stage_direct(ring.hi(buf, 1), ring.lo(buf, 1), wt, C, s * KS, Ident{});  // (d', i) = W(i, d')
-    stage_trans(ring.hi(buf, 2), ring.lo(buf, 2), u, D, s * KS, Ident{});    // (v, i) = U(i, v)
-    slice_publish();
-    if (threadIdx.x == 0) {
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-      commit(&ring.bars[buf]);
-    }
-  }
+  int g = 0;
+  const Src srcs[3] = {trans(kg, D), direct(wt, C), trans(u, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
+  kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+    mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+  });
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
   float* mo = ws.M + chunk * D * D;
@@ -237,18 +230,12 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   const float* qgt = ws.qgT + chunk * C * D;
   const float* hp = ws.hpre + chunk * D * D;
   int g = 0;
-  for (int s = 0; s < D / KS; ++s, ++g) {
-    const int buf = g & 1;
-    ring_acquire(ring, buf, g >> 1, ws.status);
-    stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), wt, C, s * KS, Ident{});           // (i,d) = W
-    stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), qgt, C, s * KS, Scale{p.scale});   // (i,d) = s qg
-    stage_trans(ring.hi(buf, 2), ring.lo(buf, 2), hp, D, s * KS, Ident{});           // (v,d) = h(d,v)
-    slice_publish();
-    if (threadIdx.x == 0) {
+  {
+    const Src srcs[3] = {trans(wt, C), trans(qgt, C, p.scale), trans(hp, D)};  // W, s qg, h^T
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
-      commit(&ring.bars[buf]);
-    }
+    });
   }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
@@ -264,16 +251,11 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   });
   __syncthreads();   // vnew (global) visible to the whole CTA
   const float* aqkt = ws.AqkT + chunk * C * C;
-  for (int s = 0; s < C / KS; ++s, ++g) {
-    const int buf = g & 1;
-    ring_acquire(ring, buf, g >> 1, ws.status);
-    stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), aqkt, C, s * KS, Ident{});   // (i,j) = Aqk
-    stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), vn, D, s * KS, Ident{});     // (v,j) = vnew(j,v)
-    slice_publish();
-    if (threadIdx.x == 0) {
+  {
+    const Src srcs[2] = {trans(aqkt, C), trans(vn, D)};   // (i,j) = Aqk, (v,j) = vnew(j,v)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1);
-      commit(&ring.bars[buf]);
-    }
+    });
   }
   drain(&ts.done, ph, ws.status);
   if (o) {
@@ -309,18 +291,12 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   const float* aqkt = ws.AqkT + chunk * C * C;
   const float* qgt = ws.qgT + chunk * C * D;
   int g = 0;
-  for (int s = 0; s < C / KS; ++s, ++g) {
-    const int buf = g & 1;
-    ring_acquire(ring, buf, g >> 1, ws.status);
-    stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), aqkt, C, s * KS, Ident{});          // (j,i)
-    stage_direct(ring.hi(buf, 1), ring.lo(buf, 1), qgt, C, s * KS, Scale{p.scale});    // (d,i)
-    stage_trans(ring.hi(buf, 2), ring.lo(buf, 2), doc, rs, s * KS, Ident{});           // (v,i)
-    slice_publish();
-    if (threadIdx.x == 0) {
+  {
+    const Src srcs[3] = {direct(aqkt, C), direct(qgt, C, p.scale), trans(doc, rs)};  // (j,i) (d,i) (v,i)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
-      commit(&ring.bars[buf]);
-    }
+    });
   }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
@@ -333,16 +309,11 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   });
   __syncthreads();
   const float* wt = ws.WT + chunk * C * D;
-  for (int s = 0; s < C / KS; ++s, ++g) {
-    const int buf = g & 1;
-    ring_acquire(ring, buf, g >> 1, ws.status);
-    stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), wt, C, s * KS, Scale{-1.f});   // (d,j) = -W
-    stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), dvp, D, s * KS, Ident{});       // (v,j)
-    slice_publish();
-    if (threadIdx.x == 0) {
+  {
+    const Src srcs[2] = {direct(wt, C, -1.f), trans(dvp, D)};   // (d,j) = -W, (v,j) = dvp
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1);
-      commit(&ring.bars[buf]);
-    }
+    });
   }
   drain(&ts.done, ph, ws.status);
   float* eo = ws.E + chunk * D * D;
@@ -367,17 +338,11 @@ k_tc_bwd_dvn(Problem p, Workspace ws, const float* __restrict__ dh_final) {
   Ring ring = make_ring(sm, &ts, 2);
   const float* kg = ws.kg + chunk * C * D;
   const float* dhn = (c + 1 < p.nc) ? ws.dh + (chunk + 1) * D * D : dh_final + bh * D * D;
-  for (int s = 0; s < D / KS; ++s) {
-    const int buf = s & 1;
-    ring_acquire(ring, buf, s >> 1, ws.status);
-    stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), kg, D, s * KS, Ident{});    // (i,d)
-    stage_trans(ring.hi(buf, 1), ring.lo(buf, 1), dhn, D, s * KS, Ident{});    // (v,d)
-    slice_publish();
-    if (threadIdx.x == 0) {
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-      commit(&ring.bars[buf]);
-    }
-  }
+  int g = 0;
+  const Src srcs[2] = {direct(kg, D), trans(dhn, D)};   // (i,d), (v,d)
+  kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+  });
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
   const float* dvp = ws.dvp + chunk * C * D;

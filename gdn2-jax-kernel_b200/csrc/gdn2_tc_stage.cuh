@@ -25,7 +25,7 @@ struct Scale {
 // tile(r, k) = src[r * ld + k0 + k], r < 128, k < 32.  A warp covers 8 rows x
 // 4 column chunks, so its 16-byte shared stores span all 8 bank quads.
 template <class F>
-__device__ __forceinline__ void stage_direct(float* hi, float* lo, const float* __restrict__ src,
+__device__ __forceinline__ void stage_direct(float* hi, float* lo, const float* src,
                                              long ld, int k0, F f) {
 #pragma unroll
   for (int it = 0; it < 1024 / kThreads; ++it) {
@@ -42,7 +42,7 @@ __device__ __forceinline__ void stage_direct(float* hi, float* lo, const float* 
 // the source and transposed in registers.  The store order of the 4 tile rows
 // is rotated by lane so a warp's stores spread over the 8 bank quads.
 template <class F>
-__device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* __restrict__ src,
+__device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* src,
                                             long ld, int k0, F f) {
   const int e = threadIdx.x;                       // 256 blocks of 4 x 4
   const int rb = (e & 7) + ((e >> 5) & 3) * 8;     // 32 row blocks
@@ -69,35 +69,38 @@ __device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* _
 struct Frag {
   float4 v[4];
 };
-__device__ __forceinline__ void load_direct(Frag& f, const float* __restrict__ src, long ld, int k0) {
+__device__ __forceinline__ void load_direct(Frag& f, const float* src, long ld, int k0) {
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int e = threadIdx.x + it * kThreads;
     const int lane = e & 31, w = e >> 5;
     const int r = (w & 15) * 8 + (lane & 7);
     const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
-    f.v[it] = __ldg(reinterpret_cast<const float4*>(src + r * ld + k0 + c));
+    f.v[it] = *reinterpret_cast<const float4*>(src + r * ld + k0 + c);
   }
 }
-__device__ __forceinline__ void store_direct(float* hi, float* lo, const Frag& f) {
+__device__ __forceinline__ float4 scl(float4 v, float s) {
+  return make_float4(s * v.x, s * v.y, s * v.z, s * v.w);
+}
+__device__ __forceinline__ void store_direct(float* hi, float* lo, const Frag& f, float sc = 1.f) {
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int e = threadIdx.x + it * kThreads;
     const int lane = e & 31, w = e >> 5;
     const int r = (w & 15) * 8 + (lane & 7);
     const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
-    st_split4(hi, lo, r, c, KS, f.v[it]);
+    st_split4(hi, lo, r, c, KS, scl(f.v[it], sc));
   }
 }
-__device__ __forceinline__ void load_trans(Frag& f, const float* __restrict__ src, long ld, int k0) {
+__device__ __forceinline__ void load_trans(Frag& f, const float* src, long ld, int k0) {
   const int e = threadIdx.x;
   const int rb = (e & 7) + ((e >> 5) & 3) * 8;
   const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
   const float* p = src + (long)(k0 + kb * 4) * ld + rb * 4;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) f.v[j] = __ldg(reinterpret_cast<const float4*>(p + j * ld));
+  for (int j = 0; j < 4; ++j) f.v[j] = *reinterpret_cast<const float4*>(p + j * ld);
 }
-__device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f) {
+__device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f, float sc = 1.f) {
   const int e = threadIdx.x;
   const int rb = (e & 7) + ((e >> 5) & 3) * 8;
   const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
@@ -109,7 +112,7 @@ __device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f)
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int j = (t + rot) & 3;
-    st_split4(hi, lo, r0 + j, c0, KS, j == 0 ? t0 : (j == 1 ? t1 : (j == 2 ? t2 : t3)));
+    st_split4(hi, lo, r0 + j, c0, KS, scl(j == 0 ? t0 : (j == 1 ? t1 : (j == 2 ? t2 : t3)), sc));
   }
 }
 
@@ -185,6 +188,60 @@ __device__ __forceinline__ void kloop(Ring& ring, int& g, int* err, St stage, Is
   }
 }
 
+// A float32 operand source for the prefetching K loop: tile(r, k) =
+// sc * p[r*ld + k] (trans = false) or sc * p[k*ld + r] (trans = true).
+struct Src {
+  const float* p;
+  long ld;
+  float sc;
+  bool trans;
+};
+__device__ __forceinline__ Src direct(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, false}; }
+__device__ __forceinline__ Src trans(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, true}; }
+__device__ __forceinline__ void src_load(const Src& s, int k0, Frag& f) {
+  if (s.trans) load_trans(f, s.p, s.ld, k0);
+  else load_direct(f, s.p, s.ld, k0);
+}
+__device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, const Frag& f) {
+  if (s.trans) store_trans(hi, lo, f, s.sc);
+  else store_direct(hi, lo, f, s.sc);
+}
+
+// K = 128 pass over NOP float32 sources with register double-buffering: the
+// loads of slice s+1 are in flight while slice s is split, stored and issued.
+// Operand slot o of the ring holds source o; extra(buf, s) may stage more
+// slots synchronously (e.g. products of several input tensors).
+template <int NOP, class Ex, class Is>
+__device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src (&src)[NOP],
+                                         Ex extra, Is issue) {
+  Frag fa[NOP], fb[NOP];
+#pragma unroll
+  for (int o = 0; o < NOP; ++o) src_load(src[o], 0, fa[o]);
+#pragma unroll
+  for (int s = 0; s < 128 / KS; ++s) {
+    Frag* cur = (s & 1) ? fb : fa;
+    Frag* nxt = (s & 1) ? fa : fb;
+    if (s + 1 < 128 / KS) {
+#pragma unroll
+      for (int o = 0; o < NOP; ++o) src_load(src[o], (s + 1) * KS, nxt[o]);
+    }
+    const int buf = g & 1;
+    ring_acquire(ring, buf, g >> 1, err);
+#pragma unroll
+    for (int o = 0; o < NOP; ++o) src_store(src[o], ring.hi(buf, o), ring.lo(buf, o), cur[o]);
+    extra(buf, s);
+    slice_publish();
+    if (threadIdx.x == 0) {
+      issue(buf, s);
+      commit(&ring.bars[buf]);
+    }
+    ++g;
+  }
+}
+struct NoExtra {
+  __device__ __forceinline__ void operator()(int, int) const {}
+};
+
 // Wait for every MMA issued so far (commit to `bar`, then all threads wait).
 __device__ __forceinline__ void drain(uint64_t* bar, uint32_t& phase, int* err) {
   if (threadIdx.x == 0) commit(bar);
@@ -205,6 +262,35 @@ __device__ __forceinline__ void for_acc(uint32_t tmem, int col0, Fn fn) {
     float v[16];
     tmem_ld16(lane_quarter_addr(tmem, col0 + c), v);
     fn(row, c, v);
+  }
+}
+
+// Epilogue staging through shared memory: a 128 x 128 accumulator copied
+// to a padded row-major tile (ld = TLD) so the global reads and writes of the
+// epilogue can be coalesced.  TRANS stores the transpose (tile[c][r]).
+constexpr int TLD = 132;
+constexpr int TILE_FLOATS = 128 * TLD;
+template <bool TRANS>
+__device__ __forceinline__ void acc_to_smem(uint32_t tmem, int col0, float* t) {
+  for_acc<128>(tmem, col0, [&](int row, int c, const float* v) {
+    if (!TRANS) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(t + row * TLD + c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) t[(c + j) * TLD + row] = v[j];
+    }
+  });
+}
+// fn(r, c) for every row r < 128 and column group c = 0, 4, ..., 124; a warp
+// covers one row, so global accesses at (r, c..c+3) are coalesced.
+template <class F>
+__device__ __forceinline__ void for_tile(F fn) {
+#pragma unroll 4
+  for (int it = 0; it < 128 * 32 / kThreads; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    fn(e >> 5, (e & 31) * 4);
   }
 }
 
