@@ -84,6 +84,11 @@ int run_fwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
   auto c = [](const void* x) { return static_cast<const T*>(x); };
   cudaError_t e;
   hook().begin(kStageFwdIntra, s);
+  if (BT == 128 && D == 128) {
+    e = launch_tc_fwd_intra<T>(c(q), c(k), c(v), c(w), c(b), c(g), p, ws, s);
+    hook().end(kStageFwdIntra, s);
+    return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "tc_fwd_intra");
+  }
 #define GDN2_CASE(CC, DD)                                                                  \
   if (BT == CC && D == DD)                                                                  \
     e = launch_fwd_intra<T, CC, DD>(c(q), c(k), c(v), c(w), c(b), c(g), p, ws, s);          \

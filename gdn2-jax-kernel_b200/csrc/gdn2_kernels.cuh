@@ -86,6 +86,108 @@ __device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, float
   }
 }
 
+// Column-wise inclusive prefix sum of a C x D tile held row-major in shared
+// memory (ld = D).  256 threads: each column split into 256/D row segments.
+template <int C, int D>
+__device__ __forceinline__ void column_cumsum(float* s, float* tot) {
+  constexpr int NSEG = kThreads / D;
+  constexpr int RS = C / NSEG;
+  const int d = threadIdx.x % D, seg = threadIdx.x / D;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int r = seg * RS; r < (seg + 1) * RS; ++r) acc += s[r * D + d];
+  tot[seg * D + d] = acc;
+  __syncthreads();
+  float off = 0.f;
+  for (int sg = 0; sg < seg; ++sg) off += tot[sg * D + d];
+#pragma unroll 8
+  for (int r = seg * RS; r < (seg + 1) * RS; ++r) {
+    off += s[r * D + d];
+    s[r * D + d] = off;
+  }
+  __syncthreads();
+}
+
+// wy_inverse_T for C = 128 with the last doubling level (two 64 x 64 x 64
+// products) on register tiles.  `tmp` needs 4096 floats, `scr` 2 * 64 * 68.
+__device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr,
+                                                float clip) {
+  constexpr int MBK = 16, C = 128, H = 64, LY = 68;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane < MBK) {
+    const int o = warp * MBK, jj = lane;
+    float x[MBK];
+#pragma unroll
+    for (int r = 0; r < MBK; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int t = 0; t < r; ++t) s = fmaf(S[(o + t) * ld + o + r], x[t], s);
+      x[r] = (r < jj) ? 0.f : (r == jj ? san(1.f - s, clip) : san(-s, clip));
+    }
+    __syncwarp(0x0000ffffu);
+#pragma unroll
+    for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int s = 2 * MBK; s < C; s *= 2) {
+    const int half = s / 2, per = half * half, total = (C / s) * per;
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
+      const int o = beta * s;
+      float acc = 0.f;
+      for (int kk = j; kk < half; ++kk)
+        acc = fmaf(S[(o + kk) * ld + o + half + i], S[(o + j) * ld + o + kk], acc);
+      tmp[beta * per + j * half + i] = san(acc, clip);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
+      const int o = beta * s;
+      float acc = 0.f;
+      for (int kk = 0; kk <= i; ++kk)
+        acc = fmaf(S[(o + half + kk) * ld + o + half + i], tmp[beta * per + j * half + kk], acc);
+      S[(o + j) * ld + o + half + i] = san(-acc, clip);
+    }
+    __syncthreads();
+  }
+  // last level: T10 = M(64.., 0..63), A00 = A(0..63, 0..63), A11 = A(64.., 64..)
+  float* y = scr;             // y[k][j] = A00(k, j)   (row-major copy)
+  float* t = scr + H * LY;    // t[k][j] = tmp(k, j)
+  for (int e = threadIdx.x; e < H * H; e += kThreads) {
+    const int j = e / H, kk = e % H;
+    y[kk * LY + j] = S[j * ld + kk];
+  }
+  __syncthreads();
+  using T64 = Tile<64, 64, 4, 4>;
+  {
+    T64 tt;
+    tt.zero();
+    tt.mma(S + H, ld, y, LY, 0, H);             // X(i,k) = S[k*ld + 64 + i] = T10(i,k)
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      float o4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) o4[q] = san(tt.acc[ii][q], clip);
+      store_vec<4>(t + (tt.r0 + ii) * LY + tt.c0, o4);
+    }
+  }
+  __syncthreads();
+  {
+    T64 tt;
+    tt.zero();
+    tt.mma(S + H * ld + H, ld, t, LY, 0, H);    // X(i,k) = A11(i,k)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float o4[4];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) o4[ii] = san(-tt.acc[ii][q], clip);
+      store_vec<4>(S + (tt.c0 + q) * ld + H + tt.r0, o4);
+    }
+  }
+  __syncthreads();
+}
+
 // Reverse (suffix) column sum of a C x D tile in shared memory (ld = D),
 // the in-chunk reverse cumsum of gdn2_bwd.py:32-41.  `tot` >= 256 floats.
 template <int C, int D>
@@ -136,6 +238,9 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,
                              T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
                              cudaStream_t s, const LaunchHook& hook, bool skip12 = false);
+template <typename T>
+cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
+                                const T* g, const Problem& p, const Workspace& ws, cudaStream_t s);
 template <typename T>
 cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w, const T* b,
                                   const float* dout, const float* dh_final, T* dv_out, T* dw_out,

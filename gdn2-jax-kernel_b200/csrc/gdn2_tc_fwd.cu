@@ -1,0 +1,349 @@
+// Tensor-core (tcgen05, 3xTF32) intra-chunk forward of the chunk = head dim =
+// 128 path: reference Kernels A, B, C (gdn2_fwd.py:99-139, 173-260, 263-330).
+// Same workspace contract as k_fwd_intra (gdn2_fwd.cu).
+//
+// Chunk scores.  Aqk(i,j) = scale sum_d q_id k_jd e^{gc_id - gc_jd} for j <= i
+// (Akk likewise with b k on the left, j < i).  For the column block J of 32
+// columns with first row r = 32 J:
+//     e^{gc_i - gc_j} = e^{gc_i - gc_r} e^{gc_r - gc_j},
+// so block J is one product of A_J(i) = x_i e^{gc_i - gc_r} (rows i >= r, every
+// factor <= 1 for g <= 0) and B_J(j) = k_j e^{gc_r - gc_j} (j inside block J,
+// factor <= e^{spread of the block}).  A chunk whose g has a positive entry,
+// or whose 32-row spread of gc exceeds 80 (the factor could leave the float
+// range), takes the exact elementwise form with the reference's +-20 clip; for
+// g <= 0 the clip at -20 changes a term by < e^-20.
+#include "gdn2_kernels.cuh"
+#include "gdn2_tc_stage.cuh"
+
+// Optional per-phase cycle counts of one CTA (build with -DGDN2_PHASE_TIMING;
+// the counts are printed by that CTA).  Compiled out otherwise.
+#ifdef GDN2_PHASE_TIMING
+#include <cstdio>
+#define GDN2_TMARK(i) \
+  do { if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) tmark[i] = clock64(); } while (0)
+#else
+#define GDN2_TMARK(i) do { } while (0)
+#endif
+
+namespace gdn2 {
+
+using namespace tc;
+
+namespace {
+
+constexpr int C = 128, D = 128;
+
+struct TcSmemF {
+  float red[264];
+  uint64_t bars[2];
+  uint64_t done;
+  uint32_t tmem;
+};
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void sts4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+}  // namespace
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+               const T* __restrict__ w, const T* __restrict__ b, const T* __restrict__ g,
+               Problem p, Workspace ws) {
+  extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(16) TcSmemF ts;
+#ifdef GDN2_PHASE_TIMING
+  long long tmark[8];
+#endif
+  const size_t chunk = blockIdx.x;
+  const int c = (int)(chunk % p.nc);
+  const size_t bh = chunk / p.nc;
+  const int h = (int)(bh % p.H), bb = (int)(bh / p.H);
+  const long rs = p.row_stride();
+  const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
+  const T *qc = q + off, *kc = k + off, *vc = v + off, *wc = w + off, *bc = b + off,
+          *gcp = g + off;
+  // shared memory plan (floats): phases 0-2 keep gc in [0, 16384); the score
+  // ring, then the transposed score tiles and the solve, follow it; phase 3
+  // reuses everything for its ring.
+  float* sgc = sm;
+  float* ringA = sm + C * D;                       // 2 buffers x 2 operands x slice
+  float* bsl = ringA + 2 * 2 * 2 * SLICE_FLOATS;   // 2 buffers x (hi, lo) x 32 x 32
+  float* t0 = sm + C * D;                          // after the score products
+  float* S = t0 + TILE_FLOATS;
+  float* tmp = S + TILE_FLOATS;                    // 4096 floats
+
+  if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 256);
+  if (threadIdx.x == 0) {
+    mbar_init(&ts.bars[0], 1);
+    mbar_init(&ts.bars[1], 1);
+    mbar_init(&ts.done, 1);
+    fence_mbar_init();
+  }
+
+  GDN2_TMARK(0);
+  // ---- phase 0: gc = in-chunk cumsum of g (gdn2_fwd.py:105-107), kg, qg
+#pragma unroll 8
+  for (int it = 0; it < C * D / 4 / kThreads; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const int r = e >> 5, cc = (e & 31) * 4;
+    sts4(sgc + r * D + cc, ld4<T>(gcp + r * rs + cc));
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = ts.tmem;
+  float gpos = -1.f;
+  for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[e]);
+  const float gmax = block_max(gpos, ts.red);
+  column_cumsum<C, D>(sgc, ts.red);
+  float spread = 0.f;
+  for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
+    const int J = e / D, d = e % D;
+    spread = fmaxf(spread, fabsf(sgc[(32 * J) * D + d] - sgc[(32 * J + 31) * D + d]));
+  }
+  const bool exact = gmax > 0.f || block_max(spread, ts.red) > 80.f || spread != spread;
+  {
+    float* gco = ws.gc + chunk * C * D;
+    for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4) sts4(gco + e, lds4(sgc + e));
+    if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * D + threadIdx.x], p.clip);
+    float* kgo = ws.kg + chunk * C * D;
+    const float* gl = sgc + (C - 1) * D;
+    float* tq = sm + C * D;   // free until the score products start
+    for_tile([&](int i, int d) {
+      const float4 kv = ld4<T>(kc + i * rs + d), qv = ld4<T>(qc + i * rs + d);
+      const float4 gi = lds4(sgc + i * D + d), l4 = lds4(gl + d);
+      sts4(kgo + i * D + d, make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
+                                        san(kv.y * __expf(l4.y - gi.y), p.clip),
+                                        san(kv.z * __expf(l4.z - gi.z), p.clip),
+                                        san(kv.w * __expf(l4.w - gi.w), p.clip)));
+      tq[(d + 0) * TLD + i] = san(qv.x * __expf(gi.x), p.clip);
+      tq[(d + 1) * TLD + i] = san(qv.y * __expf(gi.y), p.clip);
+      tq[(d + 2) * TLD + i] = san(qv.z * __expf(gi.z), p.clip);
+      tq[(d + 3) * TLD + i] = san(qv.w * __expf(gi.w), p.clip);
+    });
+    __syncthreads();
+    float* qgo = ws.qgT + chunk * C * D;
+    for_tile([&](int d, int i) { sts4(qgo + d * C + i, lds4(tq + d * TLD + i)); });
+    __syncthreads();
+  }
+
+  GDN2_TMARK(1);
+  Ring ring;
+  ring.base = ringA;
+  ring.bars = ts.bars;
+  ring.phase[0] = ring.phase[1] = 0;
+  ring.nop = 2;
+  int gs = 0;
+  uint32_t ph = 0;
+  float* aqkT = ws.AqkT + chunk * C * C;
+  if (!exact) {
+    // ---- phase 1: scores.  Outer loop over 32-wide slices of d (q, k, b of
+    // the slice held in registers, the next slice prefetched), inner loop
+    // over the four column blocks J.
+    float4 qa[4], ka[4], ba[4], qn[4], kn[4], bn[4];
+    auto rc_of = [&](int it, int& i, int& cc) {
+      const int e = threadIdx.x + it * kThreads;
+      const int lane = e & 31, wq = e >> 5;
+      i = (wq & 15) * 8 + (lane & 7);
+      cc = ((wq >> 4) * 4 + (lane >> 3)) * 4;
+    };
+    auto load_qkb = [&](int s, float4* qx, float4* kx, float4* bx) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        int i, cc;
+        rc_of(it, i, cc);
+        const int d = s * KS + cc;
+        qx[it] = ld4<T>(qc + i * rs + d);
+        kx[it] = ld4<T>(kc + i * rs + d);
+        bx[it] = ld4<T>(bc + i * rs + d);
+      }
+    };
+    load_qkb(0, qa, ka, ba);
+#pragma unroll
+    for (int s = 0; s < D / KS; ++s) {
+      float4* qx = (s & 1) ? qn : qa;
+      float4* kx = (s & 1) ? kn : ka;
+      float4* bx = (s & 1) ? bn : ba;
+      if (s + 1 < D / KS) {
+        if (s & 1) load_qkb(s + 1, qa, ka, ba);
+        else load_qkb(s + 1, qn, kn, bn);
+      }
+#pragma unroll 1
+      for (int J = 0; J < 4; ++J, ++gs) {
+        const int r = 32 * J;
+        const int buf = gs & 1;
+        ring_acquire(ring, buf, gs >> 1, ws.status);
+        float* bhi = bsl + buf * 2 * 32 * KS;
+        float* blo = bhi + 32 * KS;
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          int i, cc;
+          rc_of(it, i, cc);
+          const int d = s * KS + cc;
+          float4 aq = make_float4(0.f, 0.f, 0.f, 0.f), ak = aq;
+          if (i >= r) {
+            const float4 gi = lds4(sgc + i * D + d), gr = lds4(sgc + r * D + d);
+            const float e0 = __expf(gi.x - gr.x), e1 = __expf(gi.y - gr.y),
+                        e2 = __expf(gi.z - gr.z), e3 = __expf(gi.w - gr.w);
+            const float4 qv = qx[it], kv = kx[it], bv = bx[it];
+            aq = make_float4(qv.x * e0, qv.y * e1, qv.z * e2, qv.w * e3);
+            ak = make_float4(bv.x * kv.x * e0, bv.y * kv.y * e1, bv.z * kv.z * e2, bv.w * kv.w * e3);
+          }
+          st_split4(ring.hi(buf, 0), ring.lo(buf, 0), i, cc, KS, aq);
+          st_split4(ring.hi(buf, 1), ring.lo(buf, 1), i, cc, KS, ak);
+        }
+        {
+          const int jj = threadIdx.x >> 3, cc = (threadIdx.x & 7) * 4, d = s * KS + cc;
+          const int j = r + jj;
+          const float4 gj = lds4(sgc + j * D + d), gr = lds4(sgc + r * D + d);
+          const float4 kv = ld4<T>(kc + j * rs + d);
+          st_split4(bhi, blo, jj, cc, KS,
+                    make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
+                                kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w)));
+        }
+        slice_publish();
+        if (threadIdx.x == 0) {
+          const Opnd B = kmajor(bhi, blo, KS);
+          mma3(tmem + r, ring.op(buf, 0), B, 32, KS / 8, s > 0);
+          mma3(tmem + 128 + r, ring.op(buf, 1), B, 32, KS / 8, s > 0);
+          commit(&ring.bars[buf]);
+        }
+      }
+    }
+  GDN2_TMARK(2);
+    drain(&ts.done, ph, ws.status);
+    acc_to_smem<true>(tmem, 0, t0);     // t0[j][i] = Aqk(i, j) / scale
+    acc_to_smem<true>(tmem, 128, S);    // S[j][i] = Akk(i, j)
+    __syncthreads();
+    for_tile([&](int j, int i) {
+      const float4 x = lds4(t0 + j * TLD + i), y = lds4(S + j * TLD + i);
+      sts4(aqkT + j * C + i,
+           make_float4(j <= i ? san(p.scale * x.x, p.clip) : 0.f, j <= i + 1 ? san(p.scale * x.y, p.clip) : 0.f,
+                       j <= i + 2 ? san(p.scale * x.z, p.clip) : 0.f, j <= i + 3 ? san(p.scale * x.w, p.clip) : 0.f));
+      sts4(S + j * TLD + i,
+           make_float4(j < i ? san(y.x, p.clip) : 0.f, j < i + 1 ? san(y.y, p.clip) : 0.f,
+                       j < i + 2 ? san(y.z, p.clip) : 0.f, j < i + 3 ? san(y.w, p.clip) : 0.f));
+    });
+  } else {
+    // exact elementwise form with the +-20 exponent clip (gdn2_fwd.py:124-139)
+    for (int e = threadIdx.x; e < C * C; e += kThreads) {
+      const int i = e % C, j = e / C;
+      float sq = 0.f, sk = 0.f;
+      if (j <= i) {
+        for (int d = 0; d < D; ++d) {
+          const float ed = __expf(fminf(fmaxf(sgc[i * D + d] - sgc[j * D + d], -20.f), 20.f));
+          const float kj = to_f<T>(kc[j * rs + d]) * ed;
+          sq = fmaf(to_f<T>(qc[i * rs + d]), kj, sq);
+          sk = fmaf(to_f<T>(bc[i * rs + d]) * to_f<T>(kc[i * rs + d]), kj, sk);
+        }
+      }
+      aqkT[j * C + i] = (j <= i) ? san(p.scale * sq, p.clip) : 0.f;
+      S[j * TLD + i] = (j < i) ? san(sk, p.clip) : 0.f;
+    }
+  }
+  __syncthreads();
+
+  GDN2_TMARK(3);
+  // ---- phase 2: A = (I + Akk)^-1 on the transpose (gdn2_fwd.py:173-260)
+  wy_inverse_T128(S, TLD, tmp, t0, p.clip);
+  GDN2_TMARK(4);
+  float* at = ws.AT + chunk * C * C;
+  for_tile([&](int j, int i) { sts4(at + j * C + i, lds4(S + j * TLD + i)); });
+  fence_before_sync();
+  __syncthreads();   // A in global memory for the staging below; smem reusable
+  fence_after_sync();
+
+  GDN2_TMARK(5);
+  // ---- phase 3: W = A (b k e^gc), U = A (w v)  (gdn2_fwd.py:278-282)
+  const float* gcg = ws.gc + chunk * C * D;
+  ring.base = sm;
+  ring.nop = 3;
+  {
+    // b, k, g-cumsum, w, v rows of the next slice are loaded while the current
+    // slice is stored and issued.
+    Frag fb, fk, fg, fw, fv;
+    auto ld_rows = [&](int sl) {
+      const int e = threadIdx.x;
+      const int rb = (e & 7) + ((e >> 5) & 3) * 8;
+      const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
+#pragma unroll
+      for (int jr = 0; jr < 4; ++jr) {
+        const int j = sl * KS + kb * 4 + jr, d = rb * 4;
+        fb.v[jr] = ld4<T>(bc + j * rs + d);
+        fk.v[jr] = ld4<T>(kc + j * rs + d);
+        fg.v[jr] = lds4(gcg + j * D + d);
+        fw.v[jr] = ld4<T>(wc + j * rs + d);
+        fv.v[jr] = ld4<T>(vc + j * rs + d);
+      }
+    };
+    ld_rows(0);
+    const Src srcs[1] = {trans(at, C)};   // (i, j) = A(i, j)
+    kloop_pf(ring, gs, ws.status, srcs,
+             [&](int buf, int s) {
+               Frag kb, wv;
+#pragma unroll
+               for (int jr = 0; jr < 4; ++jr) {
+                 const float4 bv = fb.v[jr], kv = fk.v[jr], g4 = fg.v[jr], w4 = fw.v[jr], v4 = fv.v[jr];
+                 kb.v[jr] = make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
+                                        bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
+                 wv.v[jr] = make_float4(w4.x * v4.x, w4.y * v4.y, w4.z * v4.z, w4.w * v4.w);
+               }
+               store_trans(ring.hi(buf, 1), ring.lo(buf, 1), kb);   // (d, j) = kb(j, d)
+               store_trans(ring.hi(buf, 2), ring.lo(buf, 2), wv);   // (v, j) = wv(j, v)
+               if (s + 1 < C / KS) ld_rows(s + 1);
+             },
+             [&](int buf, int s) {
+               mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+               mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+             });
+  }
+  GDN2_TMARK(6);
+  drain(&ts.done, ph, ws.status);
+  float* u0 = sm;
+  float* u1 = sm + TILE_FLOATS;
+  acc_to_smem<true>(tmem, 0, u0);       // u0[d][i] = W(i, d)
+  acc_to_smem<false>(tmem, 128, u1);    // u1[i][d] = U(i, d)
+  __syncthreads();
+  float* wt = ws.WT + chunk * C * D;
+  float* uo = ws.U + chunk * C * D;
+  for_tile([&](int r, int cc) {
+    const float4 x = lds4(u0 + r * TLD + cc), y = lds4(u1 + r * TLD + cc);
+    sts4(wt + r * C + cc, make_float4(san(x.x, p.clip), san(x.y, p.clip), san(x.z, p.clip), san(x.w, p.clip)));
+    sts4(uo + r * D + cc, make_float4(san(y.x, p.clip), san(y.y, p.clip), san(y.z, p.clip), san(y.w, p.clip)));
+  });
+  GDN2_TMARK(7);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if ((threadIdx.x >> 5) == 0) tmem_free(tmem, 256);
+#ifdef GDN2_PHASE_TIMING
+  if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
+    printf("fwd_intra phases: %lld %lld %lld %lld %lld %lld %lld\n", tmark[1] - tmark[0],
+           tmark[2] - tmark[1], tmark[3] - tmark[2], tmark[4] - tmark[3], tmark[5] - tmark[4],
+           tmark[6] - tmark[5], tmark[7] - tmark[6]);
+#endif
+}
+
+template <typename T>
+cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
+                                const T* g, const Problem& p, const Workspace& ws, cudaStream_t s) {
+  constexpr size_t smem = (size_t)(C * D + 2 * TILE_FLOATS + 4096) * sizeof(float);
+  static_assert(smem >= (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 32 * KS) * sizeof(float),
+                "score ring fits");
+  static_assert(smem >= 2 * 3 * (size_t)SLICE_BYTES, "phase-3 ring fits");
+  cudaError_t e = cudaFuncSetAttribute(k_tc_fwd_intra<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  k_tc_fwd_intra<T><<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, v, w, b, g, p, ws);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_tc_fwd_intra<float>(const float*, const float*, const float*,
+                                                const float*, const float*, const float*,
+                                                const Problem&, const Workspace&, cudaStream_t);
+template cudaError_t launch_tc_fwd_intra<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*,
+    const __nv_bfloat16*, const __nv_bfloat16*, const Problem&, const Workspace&, cudaStream_t);
+
+}  // namespace gdn2
