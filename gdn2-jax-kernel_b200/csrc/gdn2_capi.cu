@@ -136,6 +136,9 @@ int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
     e = launch_tc_bwd_intra12<T>(c(q), c(k), c(v), c(w), c(b), dout, dhf, m(dv), m(dw), p, ws,
                                  s, hook());
     if (e != cudaSuccess) return cuda_fail(e, "tc_bwd_intra");
+    e = launch_tc_bwd_intra3<T>(c(q), c(k), c(b), c(g), m(dq), m(dk), m(db), m(dg), p, ws, s,
+                                hook());
+    return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "tc_bwd_intra3");
   }
 #define GDN2_CASE(CC, DD)                                                                  \
   if (BT == CC && D == DD)                                                                  \

@@ -239,6 +239,10 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
                              T* dv, T* dw, T* db, T* dg, const Problem& p, const Workspace& ws,
                              cudaStream_t s, const LaunchHook& hook, bool skip12 = false);
 template <typename T>
+cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g, T* dq, T* dk,
+                                 T* db, T* dg, const Problem& p, const Workspace& ws,
+                                 cudaStream_t s, const LaunchHook& hook);
+template <typename T>
 cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                                 const T* g, const Problem& p, const Workspace& ws, cudaStream_t s);
 template <typename T>

@@ -305,6 +305,288 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
 }
 
 // ---------------------------------------------------------------------------
+// Backward of the chunk scores (B4, gdn2_bwd.py:248-339), the in-chunk
+// reverse cumsum (B5, gdn2_bwd.py:32-41) and the final assembly with the
+// +-1e4 sanitiser (gdn2_pipeline.py:117-135); same contract as k_bwd_intra3.
+// The four pair sums run as four passes of four 128 x 128 x 32 products, one
+// per 32-wide block with its own reference row r:
+//   dL_i = sum_J e^{gc_i - gc_rJ} sum_{j in J} dM_ij (k_j e^{gc_rJ - gc_j})
+//   dR_j = sum_I e^{gc_rI - gc_j} sum_{i in I} dM_ij (L_i e^{gc_i - gc_rI})
+// (every factor bounded for g <= 0 and a 32-row gc spread <= 80, otherwise
+// the exact elementwise form with the +-20 clip runs).  The decay derivative
+// is dgc_i += L_i dL_i, dgc_j -= k_j dR_j.  The dk and dgc partials stay in
+// registers (thread = TMEM row) across the passes.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ b,
+                const T* __restrict__ g, T* __restrict__ dq_out, T* __restrict__ dk_out,
+                T* __restrict__ db_out, T* __restrict__ dg_out, Problem p, Workspace ws) {
+  extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(16) TcSmemB ts;
+  const size_t chunk = blockIdx.x;
+  const int c = (int)(chunk % p.nc);
+  const size_t bh = chunk / p.nc;
+  const int h = (int)(bh % p.H), bb = (int)(bh / p.H);
+  const long rs = p.row_stride();
+  const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
+  const T *qc = q + off, *kc = k + off, *bc = b + off, *gcp = g + off;
+  const float* gc = ws.gc + chunk * C * D;
+  const float* pdq = ws.pdq + chunk * C * D;
+  const float* pdk = ws.pdk + chunk * C * D;
+  const float* pdb = ws.pdb + chunk * C * D;
+  const float* pdgc = ws.pdgc + chunk * C * D;
+  const float* dAqkT = ws.dAqkT + chunk * C * C;
+  const float* dAkkT = ws.dAkkT + chunk * C * C;
+  float* red = &ts.colpart[0][0];
+  float* sdg = sm;   // [C][D] after the products (ring area)
+
+  const uint32_t tmem = setup(&ts);
+  float gpos = -1.f;
+#pragma unroll 8
+  for (int it = 0; it < C * D / 4 / kThreads; ++it) {
+    const int e = threadIdx.x + it * kThreads;
+    const float4 g4 = ld4<T>(gcp + (e >> 5) * rs + (e & 31) * 4);
+    gpos = fmaxf(gpos, fmaxf(fmaxf(g4.x, g4.y), fmaxf(g4.z, g4.w)));
+  }
+  const float gmax = block_max(gpos, red);
+  float spread = 0.f;
+  for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
+    const int J = e / D, d = e % D;
+    spread = fmaxf(spread, fabsf(gc[(32 * J) * D + d] - gc[(32 * J + 31) * D + d]));
+  }
+  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
+
+  if (!exact) {
+    Ring ring = ring_of(sm, &ts, 2);
+    int gs = 0;
+    uint32_t ph = 0;
+    const int warp = threadIdx.x >> 5;
+    const int x = 32 * (warp & 3) + (threadIdx.x & 31);   // this thread's TMEM row
+    const int cb = (warp >> 2) * 64;                       // its first column
+    float dkr[64], dgr[64];
+#pragma unroll
+    for (int t = 0; t < 64; ++t) dkr[t] = dgr[t] = 0.f;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const bool left = pass < 2;                          // dL (row i) or dR (row j)
+      const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
+      for (int J = 0; J < 4; ++J, ++gs) {
+        const int r = 32 * J;
+        const int buf = gs & 1;
+        ring_acquire(ring, buf, gs >> 1, ws.status);
+        if (left) {
+          stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, r, Ident{});   // (i, jj) = dM(i, r+jj)
+          stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, jj) = R
+            const int j = r + kk;
+            const float4 kv = ld4<T>(kc + j * rs + d);
+            const float4 gj = ldg4(gc + j * D + d), gr = ldg4(gc + r * D + d);
+            return make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
+                               kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w));
+          });
+        } else {
+          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, r, Ident{});  // (j, ii) = dM(r+ii, j)
+          stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, ii) = L
+            const int i = r + kk;
+            const float4 gi = ldg4(gc + i * D + d), gr = ldg4(gc + r * D + d);
+            float4 lv;
+            if (pass == 2) {
+              const float4 qv = ld4<T>(qc + i * rs + d);
+              lv = make_float4(p.scale * qv.x, p.scale * qv.y, p.scale * qv.z, p.scale * qv.w);
+            } else {
+              const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4<T>(bc + i * rs + d);
+              lv = make_float4(bv.x * kv.x, bv.y * kv.y, bv.z * kv.z, bv.w * kv.w);
+            }
+            return make_float4(lv.x * __expf(gi.x - gr.x), lv.y * __expf(gi.y - gr.y),
+                               lv.z * __expf(gi.z - gr.z), lv.w * __expf(gi.w - gr.w));
+          });
+        }
+        slice_publish();
+        if (threadIdx.x == 0) {
+          mma3(tmem + 128 * J, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 0);
+          commit(&ring.bars[buf]);
+        }
+      }
+      drain(&ts.done, ph, ws.status);
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        const int c0 = cb + qd * 16;
+        float val[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) val[t] = 0.f;
+        float gx[16];
+#pragma unroll
+        for (int t = 0; t < 16; t += 4) {
+          const float4 v4 = ldg4(gc + x * D + c0 + t);
+          gx[t] = v4.x; gx[t + 1] = v4.y; gx[t + 2] = v4.z; gx[t + 3] = v4.w;
+        }
+#pragma unroll
+        for (int J = 0; J < 4; ++J) {
+          float a[16];
+          tmem_ld16(lane_quarter_addr(tmem, 128 * J + c0), a);
+          const int r = 32 * J;
+          const bool use = left ? (x >= r) : (x < r + 32);
+          if (use) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const float gr = gc[r * D + c0 + t];
+              val[t] += a[t] * __expf(left ? gx[t] - gr : gr - gx[t]);
+            }
+          }
+        }
+        float4 xa[4], xb[4];
+        if (pass == 0) {
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) xa[t / 4] = ld4<T>(qc + x * rs + c0 + t);
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) {
+            const float4 pq = ldg4(pdq + x * D + c0 + t);
+            const float* qv = &xa[t / 4].x;
+            const float* pv = &pq.x;
+            float o[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              o[u] = san(pv[u] + san(p.scale * val[t + u], p.clip), kFinalClipTc);
+              dgr[qd * 16 + t + u] += p.scale * qv[u] * val[t + u];
+            }
+            st4<T>(dq_out + off + x * rs + c0 + t, make_float4(o[0], o[1], o[2], o[3]));
+          }
+        } else if (pass == 1) {
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) {
+            xa[t / 4] = ld4<T>(kc + x * rs + c0 + t);
+            xb[t / 4] = ld4<T>(bc + x * rs + c0 + t);
+          }
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) {
+            const float4 pb = ldg4(pdb + x * D + c0 + t);
+            const float* kv = &xa[t / 4].x;
+            const float* bv = &xb[t / 4].x;
+            const float* pv = &pb.x;
+            float o[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float dbk = val[t + u];
+              o[u] = san(pv[u] + san(dbk * kv[u], p.clip), kFinalClipTc);
+              dkr[qd * 16 + t + u] = dbk * bv[u];
+              dgr[qd * 16 + t + u] += bv[u] * kv[u] * dbk;
+            }
+            st4<T>(db_out + off + x * rs + c0 + t, make_float4(o[0], o[1], o[2], o[3]));
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) xa[t / 4] = ld4<T>(kc + x * rs + c0 + t);
+#pragma unroll
+          for (int t = 0; t < 16; t += 4) {
+            const float* kv = &xa[t / 4].x;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              dkr[qd * 16 + t + u] += val[t + u];
+              dgr[qd * 16 + t + u] -= kv[u] * val[t + u];
+            }
+          }
+          if (pass == 3) {
+#pragma unroll
+            for (int t = 0; t < 16; t += 4) {
+              const float4 pk = ldg4(pdk + x * D + c0 + t);
+              const float* pv = &pk.x;
+              float o[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                o[u] = san(pv[u] + san(dkr[qd * 16 + t + u], p.clip), kFinalClipTc);
+              st4<T>(dk_out + off + x * rs + c0 + t, make_float4(o[0], o[1], o[2], o[3]));
+            }
+          }
+        }
+      }
+    }
+    // dgc total into shared memory (ring is idle after the last drain)
+    __syncthreads();
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd) {
+      const int c0 = cb + qd * 16;
+#pragma unroll
+      for (int t = 0; t < 16; t += 4) {
+        const float4 pg = ldg4(pdgc + x * D + c0 + t);
+        st4(sdg + x * D + c0 + t, pg.x + san(dgr[qd * 16 + t], p.clip),
+            pg.y + san(dgr[qd * 16 + t + 1], p.clip), pg.z + san(dgr[qd * 16 + t + 2], p.clip),
+            pg.w + san(dgr[qd * 16 + t + 3], p.clip));
+      }
+    }
+  } else {
+    // exact elementwise form (gdn2_bwd.py:298-328)
+    for (int e = threadIdx.x; e < C * D; e += kThreads) {
+      const int x = e / D, d = e % D;
+      const float kx = to_f<T>(kc[x * rs + d]), bx = to_f<T>(bc[x * rs + d]);
+      const float lq = p.scale * to_f<T>(qc[x * rs + d]), lk = bx * kx;
+      float dlq = 0.f, dlk = 0.f, drq = 0.f, drk = 0.f, dgi = 0.f, dgj = 0.f;
+      for (int y = 0; y < C; ++y) {
+        if (y <= x) {
+          const float dd = gc[x * D + d] - gc[y * D + d];
+          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
+          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
+          const float mq = dAqkT[y * C + x], mk = (y < x) ? dAkkT[y * C + x] : 0.f;
+          const float ry = to_f<T>(kc[y * rs + d]) * ed;
+          dlq = fmaf(mq, ry, dlq);
+          dlk = fmaf(mk, ry, dlk);
+          dgi += (mq * lq + mk * lk) * ry * cm;
+        }
+        if (y >= x) {
+          const float dd = gc[y * D + d] - gc[x * D + d];
+          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
+          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
+          const float mq = dAqkT[x * C + y], mk = (y > x) ? dAkkT[x * C + y] : 0.f;
+          const float lqy = p.scale * to_f<T>(qc[y * rs + d]) * ed;
+          const float lky = to_f<T>(bc[y * rs + d]) * to_f<T>(kc[y * rs + d]) * ed;
+          drq = fmaf(mq, lqy, drq);
+          drk = fmaf(mk, lky, drk);
+          dgj += (mq * lqy + mk * lky) * kx * cm;
+        }
+      }
+      dq_out[off + x * rs + d] = from_f<T>(san(pdq[e] + san(p.scale * dlq, p.clip), kFinalClipTc));
+      db_out[off + x * rs + d] = from_f<T>(san(pdb[e] + san(dlk * kx, p.clip), kFinalClipTc));
+      dk_out[off + x * rs + d] =
+          from_f<T>(san(pdk[e] + san(drq + drk + dlk * bx, p.clip), kFinalClipTc));
+      sdg[e] = pdgc[e] + san(dgi - dgj, p.clip);
+    }
+  }
+  __syncthreads();
+  column_revcumsum<C, D>(sdg, red);
+  for_tile([&](int i, int d) {
+    const float4 v4 = ldg4(sdg + i * D + d);
+    st4<T>(dg_out + off + i * rs + d,
+           san4(san4(v4, p.clip), kFinalClipTc));
+  });
+  teardown(tmem);
+}
+
+template <typename T>
+cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g, T* dq, T* dk,
+                                 T* db, T* dg, const Problem& p, const Workspace& ws,
+                                 cudaStream_t s, const LaunchHook& hook) {
+  constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES;   // ring; also holds the C x D dgc tile
+  static_assert(smem >= (size_t)C * D * sizeof(float), "dgc tile fits");
+  cudaError_t e = cudaFuncSetAttribute(k_tc_bwd_intra3<T>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  hook.begin(kStageBwdIntra3, s);
+  k_tc_bwd_intra3<T><<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, b, g, dq, dk, db, dg,
+                                                                          p, ws);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  hook.end(kStageBwdIntra3, s);
+  return cudaSuccess;
+}
+
+template cudaError_t launch_tc_bwd_intra3<float>(const float*, const float*, const float*,
+                                                 const float*, float*, float*, float*, float*,
+                                                 const Problem&, const Workspace&, cudaStream_t,
+                                                 const LaunchHook&);
+template cudaError_t launch_tc_bwd_intra3<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*,
+    __nv_bfloat16*, __nv_bfloat16*, __nv_bfloat16*, __nv_bfloat16*, const Problem&,
+    const Workspace&, cudaStream_t, const LaunchHook&);
+
+// ---------------------------------------------------------------------------
 template <typename T>
 cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w, const T* b,
                                   const float* dout, const float* dh_final, T* dv_out, T* dw_out,
