@@ -283,4 +283,25 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
                                             dv, dw, db, dg, p, ws, s);
 }
 
+int gdn2_sp_segment(int op, void* workspace, size_t workspace_bytes, const float* in, float* o,
+                    float* out, int B, int T, int H, int D, int BT, int BC, float scale,
+                    float clip, void* stream) {
+  int rc = validate(GDN2_F32, B, T, H, D, BT, BC, scale, clip);
+  if (rc) return rc;
+  if (!use_tc(BT, D))
+    return fail(GDN2_ERR_INVALID, "%ssequence parallelism needs BT = D = 128");
+  if (op < 0 || op > 2) return fail(GDN2_ERR_INVALID, "%sunknown segment op %ld", "", op);
+  if (!workspace || !out || (op == 2 && !in))
+    return fail(GDN2_ERR_INVALID, "%snull buffer pointer");
+  const bool bwd = op == 2;
+  const size_t need = gdn2_workspace_bytes(B, T, H, D, BT, bwd ? 1 : 0);
+  if (workspace_bytes < need)
+    return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
+                (long)need, (long)workspace_bytes);
+  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, bwd);
+  cudaError_t e = launch_tc_sp(op, p, ws, in, o, out, static_cast<cudaStream_t>(stream), hook());
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "sp_segment");
+}
+
 }  // extern "C"

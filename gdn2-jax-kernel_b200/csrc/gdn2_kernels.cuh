@@ -251,6 +251,11 @@ cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w
                                   const Problem& p, const Workspace& ws, cudaStream_t s,
                                   const LaunchHook& hook);
 
+// Sequence-parallel pieces (tensor-core path): op 0 segment map P = prod M_c,
+// op 1 rescan from the start state `in` + chunk outputs, op 2 backward
+// segment term from dout = `in` with zero incoming gradient.
+cudaError_t launch_tc_sp(int op, const Problem& p, const Workspace& ws, const float* in, float* o,
+                         float* out, cudaStream_t s, const LaunchHook& hook);
 // Tensor-core path (chunk = head dim = 128, float32 workspace), gdn2_tc_kernels.cu.
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,
                           float* hfinal, cudaStream_t s, const LaunchHook& hook);

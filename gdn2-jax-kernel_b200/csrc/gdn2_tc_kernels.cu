@@ -123,7 +123,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
 // 128 x 128 x 128 3xTF32 product into TMEM, then the epilogue adds the
 // constant term, sanitises, stores the state and restages it as the A tile.
 // ---------------------------------------------------------------------------
-template <bool BWD>
+// PROD (forward only) instead accumulates the segment map P = M_last ... M_first
+// from P = I with no constant term and no sanitiser, writing only P to
+// out_final (sequence parallelism).
+template <bool BWD, bool PROD = false>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __restrict__ out_final) {
   extern __shared__ __align__(128) float sm[];
@@ -137,13 +140,21 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   auto s_lo = [&](int s) { return S + s * 2 * SLICE_FLOATS + SLICE_FLOATS; };
 
   const float* src0 = init ? init + bh * D * D : nullptr;
-  if (src0) {
+  if (PROD) {
+    for (int e = threadIdx.x; e < D * D / 4; e += kThreads) {   // identity, transposed = itself
+      const int r = e / (D / 4), cc = (e % (D / 4)) * 4;
+      float4 v4 = make_float4(r == cc ? 1.f : 0.f, r == cc + 1 ? 1.f : 0.f, r == cc + 2 ? 1.f : 0.f,
+                              r == cc + 3 ? 1.f : 0.f);
+      st_split4(S + (cc / KS) * 2 * SLICE_FLOATS, S + (cc / KS) * 2 * SLICE_FLOATS + SLICE_FLOATS, r,
+                cc % KS, KS, v4);
+    }
+  } else if (src0) {
     for (int s = 0; s < D / KS; ++s) stage_trans(s_hi(s), s_lo(s), src0, D, s * KS, SanT{p.clip});
   } else {
     for (int e = threadIdx.x; e < 4 * 2 * SLICE_FLOATS / 4; e += kThreads)
       st4f(S + 4 * e, make_float4(0.f, 0.f, 0.f, 0.f));
   }
-  if (!BWD) {
+  if (!BWD && !PROD) {
     float* hp = ws.hpre + (bh * p.nc) * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) hp[e] = src0 ? san(src0[e], p.clip) : 0.f;
   }
@@ -167,7 +178,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   auto load_add = [&](int c) {
     const float* add = (BWD ? ws.E : ws.Bc) + (bh * p.nc + c) * D * D;
 #pragma unroll
-    for (int j = 0; j < 64; ++j) addv[j] = __ldg(add + (dcol0 + j) * D + vrow);
+    for (int j = 0; j < 64; ++j) addv[j] = PROD ? 0.f : __ldg(add + (dcol0 + j) * D + vrow);
   };
   load_m(BWD ? p.nc - 1 : 0);
   for (int it = 0; it < p.nc; ++it) {
@@ -189,7 +200,8 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     drain(&ts.done, ph, ws.status);
     const bool last = it == p.nc - 1;
     float* dst;
-    if (!BWD) dst = last ? (out_final ? out_final + bh * D * D : nullptr) : ws.hpre + (chunk + 1) * D * D;
+    if (PROD) dst = last ? out_final + bh * D * D : nullptr;
+    else if (!BWD) dst = last ? (out_final ? out_final + bh * D * D : nullptr) : ws.hpre + (chunk + 1) * D * D;
     else dst = ws.dh + chunk * D * D;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -199,9 +211,9 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
       float y[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        y[j] = san(x[j] + addv[q * 16 + j], p.clip);
+        y[j] = PROD ? x[j] : san(x[j] + addv[q * 16 + j], p.clip);
         if (dst) dst[(c0 + j) * D + vrow] = y[j];
-        if (BWD && last) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y[j], 1e4f);
+        if (BWD && last && out_final) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y[j], 1e4f);
       }
       const int s = c0 / KS, cc = c0 % KS;
 #pragma unroll
@@ -414,4 +426,37 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
   return cudaSuccess;
 }
 
+}  // namespace gdn2
+
+namespace gdn2 {
+cudaError_t launch_tc_sp(int op, const Problem& p, const Workspace& ws, const float* in,
+                         float* o, float* out, cudaStream_t s, const LaunchHook& hook) {
+  cudaError_t e;
+  const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
+  if (op == 0) {            // forward segment map P = prod M_c
+    if ((e = prep(k_tc_scan<false, true>, kScan)) != cudaSuccess) return e;
+    k_tc_scan<false, true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, nullptr, out);
+    return cudaGetLastError();
+  }
+  if (op == 1) {            // rescan from a given start state + chunk outputs
+    if ((e = prep(k_tc_scan<false>, kScan)) != cudaSuccess) return e;
+    if ((e = prep(k_tc_fwd_out, kRing3)) != cudaSuccess) return e;
+    hook.begin(kStageFwdScan, s);
+    k_tc_scan<false><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, in, out);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    hook.end(kStageFwdScan, s);
+    hook.begin(kStageFwdOut, s);
+    k_tc_fwd_out<<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    hook.end(kStageFwdOut, s);
+    return cudaSuccess;
+  }
+  // op == 2: backward segment term, zero incoming gradient
+  if ((e = prep(k_tc_bwd_prep, kRing3)) != cudaSuccess) return e;
+  if ((e = prep(k_tc_scan<true>, kScan)) != cudaSuccess) return e;
+  k_tc_bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, in);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  k_tc_scan<true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, nullptr, out);
+  return cudaGetLastError();
+}
 }  // namespace gdn2

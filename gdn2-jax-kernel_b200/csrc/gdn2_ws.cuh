@@ -62,6 +62,8 @@ struct Workspace {
     Workspace w{};
     size_t n = (size_t)B * H * nc;
     float* f = reinterpret_cast<float*>(((uintptr_t)p + 255) & ~(uintptr_t)255);
+    w.status = reinterpret_cast<int*>(f);   // first 256 bytes: status word
+    f += 64;
     w.base = f;
     auto take = [&](size_t per) { float* r = f; f += per * n; return r; };
     w.AqkT = take((size_t)C * C);
@@ -89,7 +91,6 @@ struct Workspace {
       w.E = take((size_t)D * D);
       w.dvp = take((size_t)C * D);
     }
-    w.status = reinterpret_cast<int*>(f);
     w.bytes = required_bytes(B, H, nc, C, D, bwd);
     return w;
   }

@@ -155,7 +155,7 @@ def _unpack_residuals(p, ws):
     B, H, D, C = p.B, p.H, p.D, p.C
     nc = p.T // C
     n = B * H * nc
-    base = (ws.data_ptr() + 255) // 256 * 256 - ws.data_ptr()
+    base = (ws.data_ptr() + 255) // 256 * 256 - ws.data_ptr() + 256   # after the status word
     f = ws[base:].view(torch.float32)
     sizes = [("AqkT", C * C), ("AT", C * C), ("WT", C * D), ("U", C * D), ("kg", C * D),
              ("qgT", C * D), ("gc", C * D), ("gcl", D), ("hpre", D * D), ("vnew", C * D)]

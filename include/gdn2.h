@@ -66,6 +66,22 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
              float* dh0, void* workspace, size_t workspace_bytes, int residuals_valid, int B,
              int T, int H, int D, int BT, int BC, float scale, float clip, void* stream);
 
+/* Sequence-parallel building blocks (no single counterpart in the reference,
+ * whose scan is serial over the whole sequence, gdn2_fwd.py:362): a rank that
+ * owns a contiguous time segment uses them on the workspace of its segment.
+ * Requires BT = D = 128.
+ *   op 0: after gdn2_fwd(save_residuals = 1), out (B,H,D,D) = the segment map
+ *         P = M_last ... M_first, where h_out = P h_in + c and c is the h_final
+ *         of the segment run from a zero state;
+ *   op 1: rescan the segment from start state `in` (B,H,D,D): rewrites the
+ *         per-chunk residual states, o (may be NULL) and out = h_final;
+ *   op 2: (backward workspace) out (B,H,D,D) = the gradient at the segment
+ *         start for a zero incoming gradient, given dout = `in`.
+ * The incoming gradient of a segment maps as g_start = P^T g_end + out. */
+int gdn2_sp_segment(int op, void* workspace, size_t workspace_bytes, const float* in, float* o,
+                    float* out, int B, int T, int H, int D, int BT, int BC, float scale,
+                    float clip, void* stream);
+
 /* Forward for callers that cannot allocate device memory (no counterpart in
  * the reference).  Same arguments and results as gdn2_fwd without the
  * workspace: the scratch lives in a fixed device array of
