@@ -317,6 +317,64 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_sp(args, rank, world, local_rank):
+    """Config 3 (B1 T131072 H8 D128 fp32, BT128 BC64) fwd+bwd, the sequence
+    split over the ranks (strong scaling: the job is fixed)."""
+    import torch
+    import torch.distributed as dist
+    from gdn2_package import gdn2_fwd
+    from gdn2_package import sequence_parallel as SP
+    from gdn2_package.synthetic import make_inputs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B, T, H, D = 1, 131072, 8, 128
+    gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP = 128, 64, 1e4
+    L = T // world
+    inp = make_inputs(B, L, H, D, seed=1000 + rank)
+    names = ("q", "k", "v", "w", "b", "g")
+    x = [torch.from_numpy(inp[n]).to(dev) for n in names]
+    do = torch.from_numpy(inp["dout"]).to(dev)
+    dhf = torch.from_numpy(inp["dh_final"]).to(dev)
+    gather = SP.dist_gather() if world > 1 else (lambda t: [t])
+
+    def step():
+        o, hf, st = SP.sp_forward(*x, inp["scale"], None, rank, gather)
+        return SP.sp_backward(st, do, dhf, gather)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    ms = float(t[0]) / args.steps
+    line = {
+        "metric": "fwd+bwd tokens/s at B1·T131072·H8·D128 fp32 (sequence parallel)",
+        "value": B * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference distributions, seeded)",
+        "config": {"workload": "config3 fwd+bwd B1 T131072 H8 D128 BT128 BC64, sequence split "
+                               f"into {world} segments", "parallelism": f"sp{world}"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -327,6 +385,9 @@ def main():
     ap.add_argument("--batch", type=int, default=CFG["B"],
                     help="per-GPU batch (profiling of smaller cases only; the benchmark is B=8)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling: skip the host-buffer leg")
+    ap.add_argument("--mode", default="dp", choices=["dp", "sp"],
+                    help="dp: config 1 per GPU (default); sp: config 3 (B1 T131072 H8) split "
+                         "over the GPUs by sequence")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -334,6 +395,19 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.mode == "sp":
+        if world > 1:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        try:
+            run_sp(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
         return
     if world > 1:
         import torch
