@@ -71,6 +71,11 @@ def bytes_per_chunk(C, D):
     }
 
 
+# DRAM bytes (read + write) per chunk from one ncu capture of config 1 at B=1
+# (384 chunks; traffic grows with the chunk count), profiles/tc_intra_kernels_config1_b1.md.
+NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 778_091, "bwd_intra2": 1_239_323, "bwd_intra3": 972_301}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -286,10 +291,15 @@ def run_ours(args, rank, world, local_rank):
     top = max(per_kernel, key=lambda s: per_kernel[s]["avg_ms"])
     hbm, tflops, kind = _peaks()
     tk = per_kernel[top]
-    roofline = {"kernel": top, "bound": "tensor", "achieved": tk["tflops"], "peak": tflops,
-                "unit": "TFLOP/s", "frac": tk["tflops"] / tflops, "traffic": None,
-                "peak_kind": kind + " bf16 dense",
-                "hbm_achieved_gbs": tk["gbs"], "hbm_frac": tk["gbs"] / hbm}
+    # Every intra-chunk kernel has ~11 algorithmic FLOP per byte, far under
+    # the tensor ridge point (bf16 peak / HBM peak ~ 250 FLOP/B): HBM bounds them.
+    traffic = NCU_TRAFFIC_PER_CHUNK.get(top)
+    roofline = {"kernel": top, "bound": "hbm", "achieved": tk["gbs"], "peak": hbm,
+                "unit": "GB/s", "frac": tk["gbs"] / hbm,
+                "traffic": traffic * nchunks if traffic else None,
+                "algorithmic_bytes": by[top] * nchunks, "peak_kind": kind + " copy bandwidth",
+                "tensor_achieved_tflops": tk["tflops"], "tensor_peak_tflops": tflops,
+                "tensor_frac": tk["tflops"] / tflops}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         _single_thread_env()
