@@ -3,8 +3,9 @@
 // Same workspace contract as k_fwd_intra (gdn2_fwd.cu).
 //
 // Chunk scores.  Aqk(i,j) = scale sum_d q_id k_jd e^{gc_id - gc_jd} for j <= i
-// (Akk likewise with b k on the left, j < i).  For the column block J of 32
-// columns with first row r = 32 J:
+// (Akk likewise with b k on the left, j < i).  For the column block J of JW
+// columns (JW = 64, or 32 when a 64-row spread of gc exceeds 80) with first
+// row r = JW J:
 //     e^{gc_i - gc_j} = e^{gc_i - gc_r} e^{gc_r - gc_j},
 // so block J is one product of A_J(i) = x_i e^{gc_i - gc_r} (rows i >= r, every
 // factor <= 1 for g <= 0) and B_J(j) = k_j e^{gc_r - gc_j} (j inside block J,
@@ -32,6 +33,11 @@ using namespace tc;
 namespace {
 
 constexpr int C = 128, D = 128;
+// threads issuing MMAs: lane 0 of warps 0 .. kIss-1, one accumulator each
+#ifndef GDN2_FWD_ISS
+#define GDN2_FWD_ISS 2
+#endif
+constexpr int kIss = GDN2_FWD_ISS;
 
 struct TcSmemF {
   float red[264];
@@ -68,16 +74,16 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   // reuses everything for its ring.
   float* sgc = sm;
   float* ringA = sm + C * D;                       // 2 buffers x 2 operands x slice
-  float* bsl = ringA + 2 * 2 * 2 * SLICE_FLOATS;   // 2 buffers x (hi, lo) x 32 x 32
+  float* bsl = ringA + 2 * 2 * 2 * SLICE_FLOATS;   // 2 buffers x (hi, lo) x 64 x 32
   float* t0 = sm + C * D;                          // after the score products
   float* S = t0 + TILE_FLOATS;
   float* tmp = S + TILE_FLOATS;                    // 4096 floats
 
   if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 256);
   if (threadIdx.x == 0) {
-    mbar_init(&ts.bars[0], 1);
-    mbar_init(&ts.bars[1], 1);
-    mbar_init(&ts.done, 1);
+    mbar_init(&ts.bars[0], kIss);
+    mbar_init(&ts.bars[1], kIss);
+    mbar_init(&ts.done, kIss);
     fence_mbar_init();
   }
 
@@ -97,12 +103,16 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[e]);
   const float gmax = block_max(gpos, ts.red);
   column_cumsum<C, D>(sgc, ts.red);
-  float spread = 0.f;
+  // largest decay-block width (64 or 32 rows) whose in-block gc spread keeps
+  // every factor e^{gc_r - gc_j} inside the float range
+  float spread = 0.f, spread64 = 0.f;
   for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
     const int J = e / D, d = e % D;
     spread = fmaxf(spread, fabsf(sgc[(32 * J) * D + d] - sgc[(32 * J + 31) * D + d]));
+    if (J < 2) spread64 = fmaxf(spread64, fabsf(sgc[(64 * J) * D + d] - sgc[(64 * J + 63) * D + d]));
   }
   const bool exact = gmax > 0.f || block_max(spread, ts.red) > 80.f || spread != spread;
+  const int JW = block_max(spread64, ts.red) <= 80.f ? 64 : 32;
   {
     float* gco = ws.gc + chunk * C * D;
     for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4) sts4(gco + e, lds4(sgc + e));
@@ -140,7 +150,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   if (!exact) {
     // ---- phase 1: scores.  Outer loop over 32-wide slices of d (q, k, b of
     // the slice held in registers, the next slice prefetched), inner loop
-    // over the four column blocks J.
+    // over the column blocks J of width JW (N = JW products: one tcgen05.mma
+    // costs about the same pipe time for N = 32 and 64, so wider blocks
+    // halve both the MMAs and the staging of the row operands).
     float4 qa[4], ka[4], ba[4], qn[4], kn[4], bn[4];
     auto rc_of = [&](int it, int& i, int& cc) {
       const int e = threadIdx.x + it * kThreads;
@@ -170,12 +182,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         else load_qkb(s + 1, qn, kn, bn);
       }
 #pragma unroll 1
-      for (int J = 0; J < 4; ++J, ++gs) {
-        const int r = 32 * J;
+      for (int J = 0; J < C / JW; ++J, ++gs) {
+        const int r = JW * J;
         const int buf = gs & 1;
         ring_acquire(ring, buf, gs >> 1, ws.status);
-        float* bhi = bsl + buf * 2 * 32 * KS;
-        float* blo = bhi + 32 * KS;
+        float* bhi = bsl + buf * 2 * 64 * KS;
+        float* blo = bhi + 64 * KS;
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
           int i, cc;
@@ -193,8 +205,8 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           st_split4(ring.hi(buf, 0), ring.lo(buf, 0), i, cc, KS, aq);
           st_split4(ring.hi(buf, 1), ring.lo(buf, 1), i, cc, KS, ak);
         }
-        {
-          const int jj = threadIdx.x >> 3, cc = (threadIdx.x & 7) * 4, d = s * KS + cc;
+        for (int jb = 0; jb < JW; jb += 32) {
+          const int jj = jb + (threadIdx.x >> 3), cc = (threadIdx.x & 7) * 4, d = s * KS + cc;
           const int j = r + jj;
           const float4 gj = lds4(sgc + j * D + d), gr = lds4(sgc + r * D + d);
           const float4 kv = ld4<T>(kc + j * rs + d);
@@ -203,16 +215,17 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                                 kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w)));
         }
         slice_publish();
-        if (threadIdx.x == 0) {
+        if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < kIss) {
           const Opnd B = kmajor(bhi, blo, KS);
-          mma3(tmem + r, ring.op(buf, 0), B, 32, KS / 8, s > 0);
-          mma3(tmem + 128 + r, ring.op(buf, 1), B, 32, KS / 8, s > 0);
+          const int who = threadIdx.x >> 5;
+          if (who == 0) mma3(tmem + r, ring.op(buf, 0), B, JW, KS / 8, s > 0);
+          if (who == kIss - 1) mma3(tmem + 128 + r, ring.op(buf, 1), B, JW, KS / 8, s > 0);
           commit(&ring.bars[buf]);
         }
       }
     }
   GDN2_TMARK(2);
-    drain(&ts.done, ph, ws.status);
+    drain_n<kIss>(&ts.done, ph, ws.status);
     acc_to_smem<true>(tmem, 0, t0);     // t0[j][i] = Aqk(i, j) / scale
     acc_to_smem<true>(tmem, 128, S);    // S[j][i] = Akk(i, j)
     __syncthreads();
@@ -279,7 +292,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     };
     ld_rows(0);
     const Src srcs[1] = {trans(at, C)};   // (i, j) = A(i, j)
-    kloop_pf(ring, gs, ws.status, srcs,
+    kloop_pf_n<kIss>(ring, gs, ws.status, srcs,
              [&](int buf, int s) {
                Frag kb, wv;
 #pragma unroll
@@ -293,13 +306,14 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                store_trans(ring.hi(buf, 2), ring.lo(buf, 2), wv);   // (v, j) = wv(j, v)
                if (s + 1 < C / KS) ld_rows(s + 1);
              },
-             [&](int buf, int s) {
-               mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-               mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+             [&](int buf, int s, int who) {
+               if (who == 0) mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+               if (who == kIss - 1)
+                 mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
              });
   }
   GDN2_TMARK(6);
-  drain(&ts.done, ph, ws.status);
+  drain_n<kIss>(&ts.done, ph, ws.status);
   float* u0 = sm;
   float* u1 = sm + TILE_FLOATS;
   acc_to_smem<true>(tmem, 0, u0);       // u0[d][i] = W(i, d)
@@ -328,8 +342,10 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 template <typename T>
 cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                                 const T* g, const Problem& p, const Workspace& ws, cudaStream_t s) {
-  constexpr size_t smem = (size_t)(C * D + 2 * TILE_FLOATS + 4096) * sizeof(float);
-  static_assert(smem >= (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 32 * KS) * sizeof(float),
+  constexpr size_t smem_rest = (size_t)(C * D + 2 * TILE_FLOATS + 4096) * sizeof(float);
+  constexpr size_t smem_scores = (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float);
+  constexpr size_t smem = smem_rest > smem_scores ? smem_rest : smem_scores;
+  static_assert(smem >= (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float),
                 "score ring fits");
   static_assert(smem >= 2 * 3 * (size_t)SLICE_BYTES, "phase-3 ring fits");
   cudaError_t e = cudaFuncSetAttribute(k_tc_fwd_intra<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,

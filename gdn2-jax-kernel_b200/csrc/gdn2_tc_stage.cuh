@@ -238,6 +238,46 @@ __device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src
     ++g;
   }
 }
+// kloop_pf with the MMA issue split over NISS issuing threads (lane 0 of
+// warps 0 .. NISS-1): issue(buf, s, who) issues issuer `who`'s share, which
+// that thread then commits.  The ring's barriers need arrival count NISS.
+template <int NISS, int NOP, class Ex, class Is>
+__device__ __forceinline__ void kloop_pf_n(Ring& ring, int& g, int* err, const Src (&src)[NOP],
+                                           Ex extra, Is issue) {
+  Frag fa[NOP], fb[NOP];
+#pragma unroll
+  for (int o = 0; o < NOP; ++o) src_load(src[o], 0, fa[o]);
+#pragma unroll
+  for (int s = 0; s < 128 / KS; ++s) {
+    Frag* cur = (s & 1) ? fb : fa;
+    Frag* nxt = (s & 1) ? fa : fb;
+    if (s + 1 < 128 / KS) {
+#pragma unroll
+      for (int o = 0; o < NOP; ++o) src_load(src[o], (s + 1) * KS, nxt[o]);
+    }
+    const int buf = g & 1;
+    ring_acquire(ring, buf, g >> 1, err);
+#pragma unroll
+    for (int o = 0; o < NOP; ++o) src_store(src[o], ring.hi(buf, o), ring.lo(buf, o), cur[o]);
+    extra(buf, s);
+    slice_publish();
+    if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < NISS) {
+      issue(buf, s, (int)(threadIdx.x >> 5));
+      commit(&ring.bars[buf]);
+    }
+    ++g;
+  }
+}
+
+// drain for NISS issuing threads (the barrier has arrival count NISS).
+template <int NISS>
+__device__ __forceinline__ void drain_n(uint64_t* bar, uint32_t& phase, int* err) {
+  if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < NISS) commit(bar);
+  mbar_wait(bar, phase, err);
+  phase ^= 1;
+  fence_after_sync();
+}
+
 struct NoExtra {
   __device__ __forceinline__ void operator()(int, int) const {}
 };
