@@ -119,22 +119,34 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * D + threadIdx.x], p.clip);
     float* kgo = ws.kg + chunk * C * D;
     const float* gl = sgc + (C - 1) * D;
+    // qg is staged transposed with an odd row stride; a warp covers 4 rows x 32
+    // columns, so the transposed scalar stores hit 32 distinct banks and the
+    // global rows are read in 128-byte pieces.
+    constexpr int QLD = C + 1;
     float* tq = sm + C * D;   // free until the score products start
-    for_tile([&](int i, int d) {
+#pragma unroll 4
+    for (int it = 0; it < C * D / 4 / kThreads; ++it) {
+      const int e = threadIdx.x + it * kThreads;
+      const int l = e & 31, wq = e >> 5;
+      const int i = (wq & 31) * 4 + (l >> 3), d = ((wq >> 5) * 8 + (l & 7)) * 4;
       const float4 kv = ld4<T>(kc + i * rs + d), qv = ld4<T>(qc + i * rs + d);
       const float4 gi = lds4(sgc + i * D + d), l4 = lds4(gl + d);
       sts4(kgo + i * D + d, make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
                                         san(kv.y * __expf(l4.y - gi.y), p.clip),
                                         san(kv.z * __expf(l4.z - gi.z), p.clip),
                                         san(kv.w * __expf(l4.w - gi.w), p.clip)));
-      tq[(d + 0) * TLD + i] = san(qv.x * __expf(gi.x), p.clip);
-      tq[(d + 1) * TLD + i] = san(qv.y * __expf(gi.y), p.clip);
-      tq[(d + 2) * TLD + i] = san(qv.z * __expf(gi.z), p.clip);
-      tq[(d + 3) * TLD + i] = san(qv.w * __expf(gi.w), p.clip);
-    });
+      tq[(d + 0) * QLD + i] = san(qv.x * __expf(gi.x), p.clip);
+      tq[(d + 1) * QLD + i] = san(qv.y * __expf(gi.y), p.clip);
+      tq[(d + 2) * QLD + i] = san(qv.z * __expf(gi.z), p.clip);
+      tq[(d + 3) * QLD + i] = san(qv.w * __expf(gi.w), p.clip);
+    }
     __syncthreads();
     float* qgo = ws.qgT + chunk * C * D;
-    for_tile([&](int d, int i) { sts4(qgo + d * C + i, lds4(tq + d * TLD + i)); });
+#pragma unroll 8
+    for (int it = 0; it < C * D / kThreads; ++it) {
+      const int e = threadIdx.x + it * kThreads;
+      qgo[e] = tq[(e >> 7) * QLD + (e & 127)];
+    }
     __syncthreads();
   }
 
@@ -206,7 +218,10 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           st_split4(ring.hi(buf, 1), ring.lo(buf, 1), i, cc, KS, ak);
         }
         for (int jb = 0; jb < JW; jb += 32) {
-          const int jj = jb + (threadIdx.x >> 3), cc = (threadIdx.x & 7) * 4, d = s * KS + cc;
+          // 8 consecutive rows per quarter-warp: 8 distinct bank quads
+          const int t = threadIdx.x;
+          const int jj = jb + (t & 7) + 8 * ((t >> 5) & 3), cc = 4 * ((t >> 3) & 3) + 16 * (t >> 7);
+          const int d = s * KS + cc;
           const int j = r + jj;
           const float4 gj = lds4(sgc + j * D + d), gr = lds4(sgc + r * D + d);
           const float4 kv = ld4<T>(kc + j * rs + d);
@@ -302,9 +317,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                                         bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
                  wv.v[jr] = make_float4(w4.x * v4.x, w4.y * v4.y, w4.z * v4.z, w4.w * v4.w);
                }
+               if (s + 1 < C / KS) ld_rows(s + 1);
                store_trans(ring.hi(buf, 1), ring.lo(buf, 1), kb);   // (d, j) = kb(j, d)
                store_trans(ring.hi(buf, 2), ring.lo(buf, 2), wv);   // (v, j) = wv(j, v)
-               if (s + 1 < C / KS) ld_rows(s + 1);
              },
              [&](int buf, int s, int who) {
                if (who == 0) mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);

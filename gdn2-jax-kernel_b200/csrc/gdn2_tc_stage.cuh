@@ -40,7 +40,8 @@ __device__ __forceinline__ void stage_direct(float* hi, float* lo, const float* 
 
 // tile(r, k) = src[(k0 + k) * ld + r]: 4 x 4 blocks read as 4 float4 rows of
 // the source and transposed in registers.  The store order of the 4 tile rows
-// is rotated by lane so a warp's stores spread over the 8 bank quads.
+// is rotated by lane so the 8 lanes of each quarter-warp (one 16-byte store
+// phase) hit 8 distinct bank quads.
 template <class F>
 __device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* src,
                                             long ld, int k0, F f) {
@@ -55,7 +56,7 @@ __device__ __forceinline__ void stage_trans(float* hi, float* lo, const float* s
   const float4 s3 = *reinterpret_cast<const float4*>(p + 3 * ld);
   const float4 t0 = make_float4(s0.x, s1.x, s2.x, s3.x), t1 = make_float4(s0.y, s1.y, s2.y, s3.y);
   const float4 t2 = make_float4(s0.z, s1.z, s2.z, s3.z), t3 = make_float4(s0.w, s1.w, s2.w, s3.w);
-  const int rot = (e >> 3) & 3;
+  const int rot = (e >> 1) & 3;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int j = (t + rot) & 3;
@@ -108,7 +109,7 @@ __device__ __forceinline__ void store_trans(float* hi, float* lo, const Frag& f,
   const float4 s0 = f.v[0], s1 = f.v[1], s2 = f.v[2], s3 = f.v[3];
   const float4 t0 = make_float4(s0.x, s1.x, s2.x, s3.x), t1 = make_float4(s0.y, s1.y, s2.y, s3.y);
   const float4 t2 = make_float4(s0.z, s1.z, s2.z, s3.z), t3 = make_float4(s0.w, s1.w, s2.w, s3.w);
-  const int rot = (e >> 3) & 3;
+  const int rot = (e >> 1) & 3;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int j = (t + rot) & 3;
