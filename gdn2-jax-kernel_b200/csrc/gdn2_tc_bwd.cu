@@ -308,8 +308,9 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
 // Backward of the chunk scores (B4, gdn2_bwd.py:248-339), the in-chunk
 // reverse cumsum (B5, gdn2_bwd.py:32-41) and the final assembly with the
 // +-1e4 sanitiser (gdn2_pipeline.py:117-135); same contract as k_bwd_intra3.
-// The four pair sums run as four passes of four 128 x 128 x 32 products, one
-// per 32-wide block with its own reference row r:
+// The four pair sums run as four passes of products 128 x 128 x JW, one per
+// JW-wide block with its own reference row r (JW = 64, or 32 when a 64-row
+// spread of gc exceeds 80):
 //   dL_i = sum_J e^{gc_i - gc_rJ} sum_{j in J} dM_ij (k_j e^{gc_rJ - gc_j})
 //   dR_j = sum_I e^{gc_rI - gc_j} sum_{i in I} dM_ij (L_i e^{gc_i - gc_rI})
 // (every factor bounded for g <= 0 and a 32-row gc spread <= 80, otherwise
@@ -350,12 +351,14 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     gpos = fmaxf(gpos, fmaxf(fmaxf(g4.x, g4.y), fmaxf(g4.z, g4.w)));
   }
   const float gmax = block_max(gpos, red);
-  float spread = 0.f;
+  float spread = 0.f, spread64 = 0.f;
   for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
     const int J = e / D, d = e % D;
     spread = fmaxf(spread, fabsf(gc[(32 * J) * D + d] - gc[(32 * J + 31) * D + d]));
+    if (J < 2) spread64 = fmaxf(spread64, fabsf(gc[(64 * J) * D + d] - gc[(64 * J + 63) * D + d]));
   }
   const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
+  const int JW = block_max(spread64, red) <= 80.f ? 64 : 32;
 
   if (!exact) {
     Ring ring = ring_of(sm, &ts, 2);
@@ -371,23 +374,23 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     for (int pass = 0; pass < 4; ++pass) {
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
       const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
-      for (int J = 0; J < 4; ++J, ++gs) {
-        const int r = 32 * J;
+      for (int sl = 0; sl < 4; ++sl, ++gs) {
+        const int J = sl * 32 / JW, r = JW * J, k0 = 32 * sl;   // K slice k0 of block J
         const int buf = gs & 1;
         ring_acquire(ring, buf, gs >> 1, ws.status);
         if (left) {
-          stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, r, Ident{});   // (i, jj) = dM(i, r+jj)
+          stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, k0, Ident{});   // (i, jj) = dM(i, k0+jj)
           stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, jj) = R
-            const int j = r + kk;
+            const int j = k0 + kk;
             const float4 kv = ld4<T>(kc + j * rs + d);
             const float4 gj = ldg4(gc + j * D + d), gr = ldg4(gc + r * D + d);
             return make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
                                kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w));
           });
         } else {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, r, Ident{});  // (j, ii) = dM(r+ii, j)
+          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, k0, Ident{});  // (j, ii) = dM(k0+ii, j)
           stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, ii) = L
-            const int i = r + kk;
+            const int i = k0 + kk;
             const float4 gi = ldg4(gc + i * D + d), gr = ldg4(gc + r * D + d);
             float4 lv;
             if (pass == 2) {
@@ -403,7 +406,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         }
         slice_publish();
         if (threadIdx.x == 0) {
-          mma3(tmem + 128 * J, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 0);
+          mma3(tmem + 128 * J, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, k0 > r);
           commit(&ring.bars[buf]);
         }
       }
@@ -422,10 +425,11 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         }
 #pragma unroll
         for (int J = 0; J < 4; ++J) {
+          if (J >= C / JW) break;
           float a[16];
           tmem_ld16(lane_quarter_addr(tmem, 128 * J + c0), a);
-          const int r = 32 * J;
-          const bool use = left ? (x >= r) : (x < r + 32);
+          const int r = JW * J;
+          const bool use = left ? (x >= r) : (x < r + JW);
           if (use) {
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
