@@ -117,6 +117,30 @@ __device__ __forceinline__ void mma3(uint32_t d_tmem, const Opnd& A, const Opnd&
   }
 }
 
+// A operand in TMEM (lane = row m, one 32-bit column per k; the tensor core
+// reads a float32 word as its tf32 head, the low 13 mantissa bits ignored).
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// mma3 with the A planes in TMEM: a_hi / a_lo are the TMEM addresses of the
+// first k column of the slice (hi and lo planes, 8 columns per k-step).
+__device__ __forceinline__ void mma3_ta(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo,
+                                        const Opnd& B, int N, int ksteps, uint32_t accumulate) {
+  const uint32_t id = idesc_tf32(128, N, 0, B.mn_major);
+  for (int s = 0; s < ksteps; ++s) {
+    const uint64_t bh = sdesc(B.hi + s * B.step, B.lbo, B.sbo);
+    const uint64_t bl = sdesc(B.lo + s * B.step, B.lbo, B.sbo);
+    mma_tf32_ta(d_tmem, a_lo + 8 * s, bh, id, (s > 0 || accumulate) ? 1u : 0u);
+    mma_tf32_ta(d_tmem, a_hi + 8 * s, bl, id, 1u);
+    mma_tf32_ta(d_tmem, a_hi + 8 * s, bh, id, 1u);
+  }
+}
+
 // ------------------------------------------------------------------ barriers
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -194,6 +218,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 16 consecutive f32 columns of this thread's TMEM lane (same address
+// rule as tmem_ld16); completion needs tmem_st_wait().
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+      "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t lane_quarter_addr(uint32_t tmem_base, int col) {

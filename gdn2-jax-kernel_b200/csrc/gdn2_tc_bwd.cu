@@ -194,91 +194,31 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   const float* dwp = ws.dWp + chunk * C * D;
   const float* dvn = ws.dv + chunk * C * D;
   const float* at = ws.AT + chunk * C * C;   // at[k*C + j] = A(j, k)
-  float* dA = ws.dAkkT + chunk * C * C;      // scratch: dA row-major, later dAkk^T
-  float* tmp = ws.E + chunk * D * D;         // scratch: tmp row-major
   const uint32_t tmem = setup(&ts);
+  // one ring (its mbarrier phases carry across the K loops); base and operand
+  // count change between loops
   Ring ring = ring_of(sm, &ts, 3);
   int g = 0;
   uint32_t ph = 0;
-  // dA = dWp kb^T + dv wv^T  (contraction over d)
-  {
-    const Src srcs[1] = {direct(dwp, D)};   // (i,d)
-    kloop_pf(ring, g, ws.status, srcs,
-             [&](int buf, int s) {
-               stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) kb
-                 const int d = s * KS + cc;
-                 const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
-                 const float4 g4 = *reinterpret_cast<const float4*>(gc + j * D + d);
-                 return make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
-                                    bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
-               });
-             },
-             [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
-  }
-  {
-    const Src srcs[1] = {direct(dvn, D)};   // (i,d)
-    kloop_pf(ring, g, ws.status, srcs,
-             [&](int buf, int s) {
-               stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) wv
-                 const int d = s * KS + cc;
-                 const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
-                 return make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
-               });
-             },
-             [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1); });
-  }
-  drain(&ts.done, ph, ws.status);
+  const int warp = threadIdx.x >> 5;
   float* t0 = sm;
   float* t1 = sm + TILE_FLOATS;
-  acc_to_smem<false>(tmem, 0, t0);
-  __syncthreads();
-  for_tile([&](int i, int c4) {
-    *reinterpret_cast<float4*>(dA + i * C + c4) = san4(lds4(t0 + i * TLD + c4), p.clip);
-  });
-  __syncthreads();
-  // tmp = san(dA A^T)  (contraction over k)
-  {
-    const Src srcs[2] = {direct(dA, C), trans(at, C)};   // (i,k) = dA, (j,k) = A(j,k)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-    });
-  }
-  drain(&ts.done, ph, ws.status);
-  acc_to_smem<false>(tmem, 128, t0);
-  __syncthreads();
-  for_tile([&](int i, int c4) {
-    *reinterpret_cast<float4*>(tmp + i * C + c4) = san4(lds4(t0 + i * TLD + c4), p.clip);
-  });
-  __syncthreads();
-  // dAkk = -(A^T tmp): (i, j) = sum_k A(k, i) tmp(k, j)
-  {
-    const Src srcs[2] = {direct(at, C), trans(tmp, C)};   // (i,k) = A(k,i), (j,k) = tmp(k,j)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-    });
-  }
-  // dkb = A^T dWp, dwv = A^T dv: (j, d) = sum_i A(i, j) X(i, d)
+  // ---- dkb = A^T dWp (TMEM 0), dwv = A^T dv (TMEM 128): (j, d) = sum_i A(i, j) X(i, d)
   {
     const Src srcs[3] = {direct(at, C), trans(dwp, D), trans(dvn, D)};   // (j,i) (d,i) (d,i)
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem + 384, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
     });
   }
   drain(&ts.done, ph, ws.status);
-  float* dAkkT = ws.dAkkT + chunk * C * C;
-  acc_to_smem<true>(tmem, 256, t0);    // t0[j][i] = acc(i, j)
-  acc_to_smem<false>(tmem, 384, t1);   // dkb (j, d)
+  acc_to_smem<false>(tmem, 0, t0);     // dkb (j, d)
+  acc_to_smem<false>(tmem, 128, t1);   // dwv (j, d)
   __syncthreads();
-  for_tile([&](int j, int i) {
-    const float4 x = lds4(t0 + j * TLD + i);
-    st4(dAkkT + j * C + i, j < i ? san(-x.x, p.clip) : 0.f, j < i + 1 ? san(-x.y, p.clip) : 0.f,
-        j < i + 2 ? san(-x.z, p.clip) : 0.f, j < i + 3 ? san(-x.w, p.clip) : 0.f);
-  });
   float *pdk = ws.pdk + chunk * C * D, *pdb = ws.pdb + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
   for_tile([&](int j, int d) {
-    const float4 x = lds4(t1 + j * TLD + d);
+    const float4 x = lds4(t0 + j * TLD + d);
     const float4 eg = exp4(ldg4(gc + j * D + d));
     const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
     const float4 pk = ldg4(pdk + j * D + d), pg = ldg4(pdgc + j * D + d);
@@ -290,16 +230,103 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
         san(pg.y + x.y * (bv.y * kv.y * eg.y), p.clip), san(pg.z + x.z * (bv.z * kv.z * eg.z), p.clip),
         san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
   });
-  __syncthreads();
-  acc_to_smem<false>(tmem, 0, t0);     // dwv (j, d)
-  __syncthreads();
   for_tile([&](int j, int d) {
-    const float4 x = lds4(t0 + j * TLD + d);
+    const float4 x = lds4(t1 + j * TLD + d);
     const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4<T>(wc + j * rs + d);
     const float4 dw = make_float4(x.x * vv.x, x.y * vv.y, x.z * vv.z, x.w * vv.w);
     const float4 dvv = make_float4(x.x * wv.x, x.y * wv.y, x.z * wv.z, x.w * wv.w);
     st4<T>(dw_out + off + j * rs + d, san4(san4(dw, p.clip), kFinalClipTc));
     st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
+  });
+  fence_before_sync();
+  __syncthreads();   // staging tiles and TMEM 0..255 free again
+  fence_after_sync();
+
+  // ---- dA = dWp kb^T + dv wv^T  (TMEM 0, contraction over d)
+  {
+    ring.base = sm;
+    ring.nop = 2;
+    {
+      const Src srcs[1] = {direct(dwp, D)};   // (i,d)
+      kloop_pf(ring, g, ws.status, srcs,
+               [&](int buf, int s) {
+                 stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) kb
+                   const int d = s * KS + cc;
+                   const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+                   const float4 g4 = ldg4(gc + j * D + d);
+                   return make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
+                                      bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
+                 });
+               },
+               [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
+    }
+    {
+      const Src srcs[1] = {direct(dvn, D)};   // (i,d)
+      kloop_pf(ring, g, ws.status, srcs,
+               [&](int buf, int s) {
+                 stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) wv
+                   const int d = s * KS + cc;
+                   const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
+                   return make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
+                 });
+               },
+               [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1); });
+    }
+  }
+  drain(&ts.done, ph, ws.status);
+  // dA = san(acc) straight into four resident K-slices (rows i, K = k) in
+  // shared memory: the B operand of the next product.
+  float* dAt = sm;                          // 4 x (hi, lo) x 128 x 32
+  for_acc<128>(tmem, 0, [&](int row, int c, const float* v) {
+    float* hi = dAt + (c / KS) * 2 * SLICE_FLOATS;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4)
+      st_split4(hi, hi + SLICE_FLOATS, row, c % KS + j, KS,
+                make_float4(san(v[j], p.clip), san(v[j + 1], p.clip), san(v[j + 2], p.clip),
+                            san(v[j + 3], p.clip)));
+  });
+  // ---- tmp^T = (dA A^T)^T: (j, i) = sum_k A(j, k) dA(i, k)  (TMEM 128)
+  {
+    ring.base = sm + 4 * 2 * SLICE_FLOATS;
+    ring.nop = 1;
+    const Src srcs[1] = {trans(at, C)};   // (j,k) = A(j,k)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      float* hi = dAt + s * 2 * SLICE_FLOATS;
+      mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, s > 0);
+    });
+  }
+  drain(&ts.done, ph, ws.status);
+  // tmp^T = san(acc) split into hi (TMEM 256..383) and lo (384..511): the A
+  // operand (rows j, K = k) of the next product.
+  for_acc<128>(tmem, 128, [&](int row, int c, const float* v) {
+    float hv[16], lv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) split(san(v[j], p.clip), hv[j], lv[j]);
+    tmem_st16(lane_quarter_addr(tmem, 256 + c), hv);
+    tmem_st16(lane_quarter_addr(tmem, 384 + c), lv);
+  });
+  tmem_st_wait();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  // ---- dAkk^T: (j, i) = -sum_k tmp(k, j) A(k, i)  (TMEM 0)
+  {
+    ring.base = sm;
+    ring.nop = 1;
+    const Src srcs[1] = {direct(at, C)};   // (i,k) = A(k,i)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3_ta(tmem, tmem + 256 + s * KS, tmem + 384 + s * KS, ring.op(buf, 0), 128, KS / 8, s > 0);
+    });
+  }
+  drain(&ts.done, ph, ws.status);
+  (void)warp;
+  float* dAkkT = ws.dAkkT + chunk * C * C;
+  acc_to_smem<false>(tmem, 0, t0);    // t0[j][i] = acc(j, i)
+  __syncthreads();
+  for_tile([&](int j, int i) {
+    const float4 x = lds4(t0 + j * TLD + i);
+    st4(dAkkT + j * C + i, j < i ? san(-x.x, p.clip) : 0.f, j < i + 1 ? san(-x.y, p.clip) : 0.f,
+        j < i + 2 ? san(-x.z, p.clip) : 0.f, j < i + 3 ? san(-x.w, p.clip) : 0.f);
   });
   teardown(tmem);
 }
