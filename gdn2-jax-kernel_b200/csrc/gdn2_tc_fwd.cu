@@ -69,9 +69,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
   const T *qc = q + off, *kc = k + off, *vc = v + off, *wc = w + off, *bc = b + off,
           *gcp = g + off;
-  // shared memory plan (floats): phases 0-2 keep gc in [0, 16384); the score
-  // ring, then the transposed score tiles and the solve, follow it; phase 3
-  // reuses everything for its ring.
+  // shared memory plan (floats): gc stays in [0, 16384) through phase 3; the
+  // score ring, then the transposed score tiles and the solve, follow it;
+  // phase 3 puts its ring after gc (A itself moves to TMEM).
   float* sgc = sm;
   float* ringA = sm + C * D;                       // 2 buffers x 2 operands x slice
   float* bsl = ringA + 2 * 2 * 2 * SLICE_FLOATS;   // 2 buffers x (hi, lo) x 64 x 32
@@ -79,7 +79,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   float* S = t0 + TILE_FLOATS;
   float* tmp = S + TILE_FLOATS;                    // 4096 floats
 
-  if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 256);
+  if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 512);
   if (threadIdx.x == 0) {
     mbar_init(&ts.bars[0], kIss);
     mbar_init(&ts.bars[1], kIss);
@@ -278,53 +278,66 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   GDN2_TMARK(4);
   float* at = ws.AT + chunk * C * C;
   for_tile([&](int j, int i) { sts4(at + j * C + i, lds4(S + j * TLD + i)); });
+  {
+    // A (rows i, K = j) split into hi (TMEM 256..383) and lo (384..511): the A
+    // operand of phase 3.  S[j * TLD + i] = A(i, j), one TMEM lane per row i.
+    const int warp = threadIdx.x >> 5;
+    const int row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
+#pragma unroll 1
+    for (int c = half * 64; c < half * 64 + 64; c += 16) {
+      float hv[16], lv[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) split(S[(c + t) * TLD + row], hv[t], lv[t]);
+      tmem_st16(lane_quarter_addr(tmem, 256 + c), hv);
+      tmem_st16(lane_quarter_addr(tmem, 384 + c), lv);
+    }
+    tmem_st_wait();
+  }
   fence_before_sync();
-  __syncthreads();   // A in global memory for the staging below; smem reusable
+  __syncthreads();   // A in TMEM; smem past the gc tile reusable
   fence_after_sync();
 
   GDN2_TMARK(5);
   // ---- phase 3: W = A (b k e^gc), U = A (w v)  (gdn2_fwd.py:278-282)
-  const float* gcg = ws.gc + chunk * C * D;
-  ring.base = sm;
-  ring.nop = 3;
+  ring.base = sm + C * D;   // after the gc tile
+  ring.nop = 2;
   {
-    // b, k, g-cumsum, w, v rows of the next slice are loaded while the current
-    // slice is stored and issued.
-    Frag fb, fk, fg, fw, fv;
+    // b, k, w, v rows of the next slice are loaded while the current slice is
+    // stored and issued.
+    Frag fb, fk, fw, fv;
+    const int rb = (threadIdx.x & 7) + ((threadIdx.x >> 5) & 3) * 8;
+    const int kb4 = ((threadIdx.x >> 3) & 3) + (threadIdx.x >> 7) * 4;
     auto ld_rows = [&](int sl) {
-      const int e = threadIdx.x;
-      const int rb = (e & 7) + ((e >> 5) & 3) * 8;
-      const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
 #pragma unroll
       for (int jr = 0; jr < 4; ++jr) {
-        const int j = sl * KS + kb * 4 + jr, d = rb * 4;
+        const int j = sl * KS + kb4 * 4 + jr, d = rb * 4;
         fb.v[jr] = ld4<T>(bc + j * rs + d);
         fk.v[jr] = ld4<T>(kc + j * rs + d);
-        fg.v[jr] = lds4(gcg + j * D + d);
         fw.v[jr] = ld4<T>(wc + j * rs + d);
         fv.v[jr] = ld4<T>(vc + j * rs + d);
       }
     };
     ld_rows(0);
-    const Src srcs[1] = {trans(at, C)};   // (i, j) = A(i, j)
-    kloop_pf_n<kIss>(ring, gs, ws.status, srcs,
+    kloop_n<kIss>(ring, gs, ws.status,
              [&](int buf, int s) {
-               Frag kb, wv;
+               Frag kbf, wv;
 #pragma unroll
                for (int jr = 0; jr < 4; ++jr) {
-                 const float4 bv = fb.v[jr], kv = fk.v[jr], g4 = fg.v[jr], w4 = fw.v[jr], v4 = fv.v[jr];
-                 kb.v[jr] = make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
-                                        bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
+                 const int j = s * KS + kb4 * 4 + jr;
+                 const float4 bv = fb.v[jr], kv = fk.v[jr], g4 = lds4(sgc + j * D + rb * 4),
+                              w4 = fw.v[jr], v4 = fv.v[jr];
+                 kbf.v[jr] = make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
+                                         bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
                  wv.v[jr] = make_float4(w4.x * v4.x, w4.y * v4.y, w4.z * v4.z, w4.w * v4.w);
                }
                if (s + 1 < C / KS) ld_rows(s + 1);
-               store_trans(ring.hi(buf, 1), ring.lo(buf, 1), kb);   // (d, j) = kb(j, d)
-               store_trans(ring.hi(buf, 2), ring.lo(buf, 2), wv);   // (v, j) = wv(j, v)
+               store_trans(ring.hi(buf, 0), ring.lo(buf, 0), kbf);  // (d, j) = kb(j, d)
+               store_trans(ring.hi(buf, 1), ring.lo(buf, 1), wv);   // (v, j) = wv(j, v)
              },
              [&](int buf, int s, int who) {
-               if (who == 0) mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-               if (who == kIss - 1)
-                 mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+               const uint32_t ah = tmem + 256 + s * KS, al = tmem + 384 + s * KS;
+               if (who == 0) mma3_ta(tmem, ah, al, ring.op(buf, 0), 128, KS / 8, s > 0);
+               if (who == kIss - 1) mma3_ta(tmem + 128, ah, al, ring.op(buf, 1), 128, KS / 8, s > 0);
              });
   }
   GDN2_TMARK(6);
@@ -345,7 +358,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  if ((threadIdx.x >> 5) == 0) tmem_free(tmem, 256);
+  if ((threadIdx.x >> 5) == 0) tmem_free(tmem, 512);
 #ifdef GDN2_PHASE_TIMING
   if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
     printf("fwd_intra phases: %lld %lld %lld %lld %lld %lld %lld\n", tmark[1] - tmark[0],
@@ -362,7 +375,8 @@ cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, 
   constexpr size_t smem = smem_rest > smem_scores ? smem_rest : smem_scores;
   static_assert(smem >= (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float),
                 "score ring fits");
-  static_assert(smem >= 2 * 3 * (size_t)SLICE_BYTES, "phase-3 ring fits");
+  static_assert(smem >= (size_t)C * D * sizeof(float) + 2 * 2 * (size_t)SLICE_BYTES,
+                "phase-3 ring fits after the gc tile");
   cudaError_t e = cudaFuncSetAttribute(k_tc_fwd_intra<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;

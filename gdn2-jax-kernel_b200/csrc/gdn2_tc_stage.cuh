@@ -270,6 +270,24 @@ __device__ __forceinline__ void kloop_pf_n(Ring& ring, int& g, int* err, const S
   }
 }
 
+// K = 128 pass whose slices are all staged by stage(buf, s) (no prefetched
+// sources), with the issue split as in kloop_pf_n.
+template <int NISS, class St, class Is>
+__device__ __forceinline__ void kloop_n(Ring& ring, int& g, int* err, St stage, Is issue) {
+#pragma unroll
+  for (int s = 0; s < 128 / KS; ++s) {
+    const int buf = g & 1;
+    ring_acquire(ring, buf, g >> 1, err);
+    stage(buf, s);
+    slice_publish();
+    if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < NISS) {
+      issue(buf, s, (int)(threadIdx.x >> 5));
+      commit(&ring.bars[buf]);
+    }
+    ++g;
+  }
+}
+
 // drain for NISS issuing threads (the barrier has arrival count NISS).
 template <int NISS>
 __device__ __forceinline__ void drain_n(uint64_t* bar, uint32_t& phase, int* err) {
