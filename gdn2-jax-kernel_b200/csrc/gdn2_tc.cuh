@@ -170,6 +170,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Bulk (non-tensor) copy global -> this CTA's shared memory, completing
+// `bytes` of transaction count on `bar`; both addresses 16-byte aligned, bytes
+// a multiple of 16.  The expecting arrival is mbar_arrive_expect_tx.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
 // Arrive on `bar` when every tcgen05.mma issued so far by this thread completes.
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile(

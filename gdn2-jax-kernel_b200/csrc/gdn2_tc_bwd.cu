@@ -173,8 +173,9 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
 // ---------------------------------------------------------------------------
 // dA = san(dWp kb^T + dv wv^T); tmp = san(dA A^T); dAkk = -(A^T tmp) * strict;
 // dkb = A^T dWp; dwv = A^T dv -> pdk, pdb, pdgc (sanitised B3 totals), dw, dv,
-// exactly as k_bwd_intra2.  dA and tmp pass through the workspace tiles dAkkT
-// and E of the chunk (both free at this point of the backward).
+// exactly as k_bwd_intra2.  dkb/dwv run first (inputs only); dA then goes from
+// TMEM into resident shared-memory B tiles, and tmp is formed transposed so
+// that its accumulator is already the TMEM A operand of dAkk^T.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   extern __shared__ __align__(128) float sm[];
   __shared__ TcSmem ts;
   const size_t chunk = blockIdx.x;
-  const uint32_t tmem = tc_setup(&ts, 256);
+  const uint32_t tmem = tc_setup(&ts, 512);
   Ring ring = make_ring(sm, &ts, 3);
   const float* kg = ws.kg + chunk * C * D;
   const float* wt = ws.WT + chunk * C * D;
@@ -86,118 +86,166 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   int g = 0;
   const Src srcs[3] = {trans(kg, D), direct(wt, C), trans(u, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
   kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-    mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
+    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);         // kg^T W
+    mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);   // kg^T U
+    mma3(tmem + 256, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);   // (kg^T W)^T
   });
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
-  float* mo = ws.M + chunk * D * D;
+  // M and M^T leave TMEM row by row as the canonical K-slices the scan
+  // streams with bulk copies (row = TMEM lane, K = column); the scan forms the
+  // lo planes itself (the tensor core reads a float32 word as its tf32 head).
   float* bo = ws.Bc + chunk * D * D;
   const float* gl = ws.gcl + chunk * D;
-  for_acc<128>(tmem, 0, [&](int row, int c, const float* v) {
-    const float dec = __expf(gl[row]);
+#pragma unroll 1
+  for (int orient = 0; orient < 2; ++orient) {
+    float* mo = ws.M + chunk * 2 * D * D + (size_t)orient * D * D;
+    for_acc<128>(tmem, orient ? 256 : 0, [&](int row, int c, const float* v) {
+      const float dec = __expf(gl[row]);
+      float* sl = mo + (c / KS) * SLICE_FLOATS;
 #pragma unroll
-    for (int j = 0; j < 16; j += 4) {
-      float4 o = make_float4(-v[j], -v[j + 1], -v[j + 2], -v[j + 3]);
-      if (row == c + j) o.x += dec;
-      if (row == c + j + 1) o.y += dec;
-      if (row == c + j + 2) o.z += dec;
-      if (row == c + j + 3) o.w += dec;
-      st4f(mo + row * D + c + j, o);
-    }
-  });
+      for (int j = 0; j < 16; j += 4) {
+        float4 o = make_float4(-v[j], -v[j + 1], -v[j + 2], -v[j + 3]);
+        if (row == c + j) o.x += dec;
+        if (row == c + j + 1) o.y += dec;
+        if (row == c + j + 2) o.z += dec;
+        if (row == c + j + 3) o.w += dec;
+        st4f(sl + canon_off(row, c % KS + j, KS) / 4, o);
+      }
+    });
+  }
   for_acc<128>(tmem, 128, [&](int row, int c, const float* v) {
 #pragma unroll
     for (int j = 0; j < 16; j += 4)
       st4f(bo + row * D + c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
   });
-  tc_teardown(tmem, 256);
+  tc_teardown(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
 // Serial affine scan over the chunks of one (batch, head).  The state is kept
-// transposed (rows = value column v, cols = key dim d) as the A operand:
+// transposed (rows = value column v, cols = key dim d) in TMEM as the A operand:
 //   forward:  h_{c+1}^T = h_c^T M_c^T + Bc_c^T   (state entering every chunk -> ws.hpre)
 //   backward: dh_c^T    = dh_{c+1}^T M_c + E_c^T (dh_pre of every chunk -> ws.dh)
-// Each step: 4 K-slices of M staged through a two-buffer ring, one
-// 128 x 128 x 128 3xTF32 product into TMEM, then the epilogue adds the
-// constant term, sanitises, stores the state and restages it as the A tile.
+// The B operand (M, or M^T backward) arrives from k_tc_affine as four 16 KB
+// canonical K-slices per chunk, streamed by bulk copies through a ring of
+// kScanSlots slots (2.5 chunks ahead).  The raw float32 slice is the hi plane;
+// each step first forms the four lo planes (x - tf32(x)) in shared memory, then
+// issues one 128 x 128 x 128 3xTF32 product; the epilogue adds the constant
+// term, sanitises, stores the state and writes it back to TMEM as hi / lo.
 // ---------------------------------------------------------------------------
 // PROD (forward only) instead accumulates the segment map P = M_last ... M_first
 // from P = I with no constant term and no sanitiser, writing only P to
 // out_final (sequence parallelism).
+constexpr int kScanSlots = 10;
+constexpr int kScanSliceBytes = SLICE_FLOATS * 4;   // one plane of one slice
+struct ScanSmem {
+  uint64_t full[kScanSlots];
+  uint64_t done;
+  uint32_t tmem;
+};
+
 template <bool BWD, bool PROD = false>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __restrict__ out_final) {
+  // shared memory: kScanSlots raw slices, then the 4 lo planes of the step
   extern __shared__ __align__(128) float sm[];
-  __shared__ TcSmem ts;
+  __shared__ ScanSmem ts;
+  float* lo = sm + kScanSlots * SLICE_FLOATS;
   const int h = blockIdx.x, bb = blockIdx.y;
   const size_t bh = (size_t)bb * p.H + h;
-  const uint32_t tmem = tc_setup(&ts, 128);
-  float* S = sm;                                     // 4 slices x (hi, lo) of 128 x 32
-  Ring ring = make_ring(sm + 4 * 2 * SLICE_FLOATS, &ts, 1);
-  auto s_hi = [&](int s) { return S + s * 2 * SLICE_FLOATS; };
-  auto s_lo = [&](int s) { return S + s * 2 * SLICE_FLOATS + SLICE_FLOATS; };
-
-  const float* src0 = init ? init + bh * D * D : nullptr;
-  if (PROD) {
-    for (int e = threadIdx.x; e < D * D / 4; e += kThreads) {   // identity, transposed = itself
-      const int r = e / (D / 4), cc = (e % (D / 4)) * 4;
-      float4 v4 = make_float4(r == cc ? 1.f : 0.f, r == cc + 1 ? 1.f : 0.f, r == cc + 2 ? 1.f : 0.f,
-                              r == cc + 3 ? 1.f : 0.f);
-      st_split4(S + (cc / KS) * 2 * SLICE_FLOATS, S + (cc / KS) * 2 * SLICE_FLOATS + SLICE_FLOATS, r,
-                cc % KS, KS, v4);
-    }
-  } else if (src0) {
-    for (int s = 0; s < D / KS; ++s) stage_trans(s_hi(s), s_lo(s), src0, D, s * KS, SanT{p.clip});
-  } else {
-    for (int e = threadIdx.x; e < 4 * 2 * SLICE_FLOATS / 4; e += kThreads)
-      st4f(S + 4 * e, make_float4(0.f, 0.f, 0.f, 0.f));
+  // TMEM: accumulator [0, 128), state hi [128, 256), state lo [256, 384)
+  if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 512);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kScanSlots; ++i) mbar_init(&ts.full[i], 1);
+    mbar_init(&ts.done, 1);
+    fence_mbar_init();
   }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = ts.tmem;
+  const int nt = p.nc * (D / KS);   // slices over the whole scan
+  auto issue = [&](int t) {          // thread 0 only
+    const int it = t / (D / KS), s = t % (D / KS);
+    const int c = BWD ? p.nc - 1 - it : it;
+    const float* src = ws.M + (bh * p.nc + c) * 2 * D * D + (BWD ? D * D : 0) + s * SLICE_FLOATS;
+    const int slot = t % kScanSlots;
+    mbar_arrive_expect_tx(&ts.full[slot], kScanSliceBytes);
+    bulk_g2s(sm + slot * SLICE_FLOATS, src, kScanSliceBytes, &ts.full[slot]);
+  };
+  if (threadIdx.x == 0)
+    for (int t = 0; t < kScanSlots && t < nt; ++t) issue(t);
+
+  const int warp = threadIdx.x >> 5;
+  const int vrow = 32 * (warp & 3) + (threadIdx.x & 31);
+  const int dcol0 = (warp >> 2) * 64;
+  // initial state (transposed): PROD -> I, else san(init) or 0
+  const float* src0 = init ? init + bh * D * D : nullptr;
   if (!BWD && !PROD) {
     float* hp = ws.hpre + (bh * p.nc) * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) hp[e] = src0 ? san(src0[e], p.clip) : 0.f;
   }
-  uint32_t ph = 0;
-  int g = 0;   // slice counter over the whole scan (ring phases)
-  // Register prefetch: this thread's share of the next M (4 slices) and of
-  // the constant term it adds in the epilogue (row v, 64 columns d).
-  const int warp = threadIdx.x >> 5;
-  const int vrow = 32 * (warp & 3) + (threadIdx.x & 31);
-  const int dcol0 = (warp >> 2) * 64;
-  Frag mf[4];
-  float addv[64];
-  auto load_m = [&](int c) {
-    const float* m = ws.M + (bh * p.nc + c) * D * D;
+#pragma unroll 1
+  for (int q = 0; q < 4; ++q) {
+    const int c0 = dcol0 + q * 16;
+    float hv[16], lv[16];
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      if (!BWD) load_direct(mf[s], m, D, s * KS);
-      else load_trans(mf[s], m, D, s * KS);
+    for (int j = 0; j < 16; ++j) {
+      const float x = PROD ? (vrow == c0 + j ? 1.f : 0.f)
+                           : (src0 ? san(src0[(c0 + j) * D + vrow], p.clip) : 0.f);
+      split(x, hv[j], lv[j]);
     }
-  };
-  auto load_add = [&](int c) {
-    const float* add = (BWD ? ws.E : ws.Bc) + (bh * p.nc + c) * D * D;
-#pragma unroll
-    for (int j = 0; j < 64; ++j) addv[j] = PROD ? 0.f : __ldg(add + (dcol0 + j) * D + vrow);
-  };
-  load_m(BWD ? p.nc - 1 : 0);
+    tmem_st16(lane_quarter_addr(tmem, 128 + c0), hv);
+    tmem_st16(lane_quarter_addr(tmem, 256 + c0), lv);
+  }
+  tmem_st_wait();
+
+  uint32_t ph = 0;
+  float addv[64];
   for (int it = 0; it < p.nc; ++it) {
     const int c = BWD ? p.nc - 1 - it : it;
     const size_t chunk = bh * p.nc + c;
-    load_add(c);
-    for (int s = 0; s < D / KS; ++s, ++g) {
-      const int buf = g & 1;
-      ring_acquire(ring, buf, g >> 1, ws.status);
-      if (!BWD) store_direct(ring.hi(buf, 0), ring.lo(buf, 0), mf[s]);   // (d, d') = M
-      else store_trans(ring.hi(buf, 0), ring.lo(buf, 0), mf[s]);         // (d', d) = M(d, d')
-      slice_publish();
-      if (threadIdx.x == 0) {
-        mma3(tmem, kmajor(s_hi(s), s_lo(s), KS), ring.op(buf, 0), 128, KS / 8, s > 0);
-        commit(&ring.bars[buf]);
+    if (!PROD) {   // this thread's share of the constant term (row v, 64 columns d)
+      const float* add = (BWD ? ws.E : ws.Bc) + chunk * D * D;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) addv[j] = add[(dcol0 + j) * D + vrow];
+    }
+    // lo planes of this step's four slices
+#pragma unroll 1
+    for (int s = 0; s < D / KS; ++s) {
+      const int t = it * (D / KS) + s, slot = t % kScanSlots;
+      mbar_wait(&ts.full[slot], (uint32_t)((t / kScanSlots) & 1), ws.status);
+      const float4* raw = reinterpret_cast<const float4*>(sm + slot * SLICE_FLOATS);
+      float4* lp = reinterpret_cast<float4*>(lo + s * SLICE_FLOATS);
+#pragma unroll
+      for (int e = threadIdx.x; e < SLICE_FLOATS / 4; e += kThreads) {
+        float4 hv, lv;
+        split4(raw[e], hv, lv);
+        lp[e] = lv;
       }
     }
-    if (it + 1 < p.nc) load_m(BWD ? c - 1 : c + 1);
-    drain(&ts.done, ph, ws.status);
+    fence_async_smem();
+    fence_before_sync();
+    __syncthreads();   // lo planes and the state in TMEM ready for the MMAs
+    fence_after_sync();
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < D / KS; ++s) {
+        const int slot = (it * (D / KS) + s) % kScanSlots;
+        const Opnd B = kmajor(sm + slot * SLICE_FLOATS, lo + s * SLICE_FLOATS, KS);
+        mma3_ta(tmem, tmem + 128 + s * KS, tmem + 256 + s * KS, B, 128, KS / 8, s > 0);
+      }
+      commit(&ts.done);
+    }
+    mbar_wait(&ts.done, ph, ws.status);
+    ph ^= 1;
+    fence_after_sync();
+    // every MMA of this step is complete: its raw slots can be refilled
+    if (threadIdx.x == 0)
+      for (int s = 0; s < D / KS; ++s) {
+        const int t = it * (D / KS) + s + kScanSlots;
+        if (t < nt) issue(t);
+      }
     const bool last = it == p.nc - 1;
     float* dst;
     if (PROD) dst = last ? out_final + bh * D * D : nullptr;
@@ -208,20 +256,23 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
       const int c0 = dcol0 + q * 16;
       float x[16];
       tmem_ld16(lane_quarter_addr(tmem, c0), x);
-      float y[16];
+      float hv[16], lv[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        y[j] = PROD ? x[j] : san(x[j] + addv[q * 16 + j], p.clip);
-        if (dst) dst[(c0 + j) * D + vrow] = y[j];
-        if (BWD && last && out_final) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y[j], 1e4f);
+        const float y = PROD ? x[j] : san(x[j] + addv[q * 16 + j], p.clip);
+        if (dst) dst[(c0 + j) * D + vrow] = y;
+        if (BWD && last && out_final) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y, 1e4f);
+        split(y, hv[j], lv[j]);
       }
-      const int s = c0 / KS, cc = c0 % KS;
-#pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        st_split4(s_hi(s), s_lo(s), vrow, cc + j, KS, make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]));
+      tmem_st16(lane_quarter_addr(tmem, 128 + c0), hv);
+      tmem_st16(lane_quarter_addr(tmem, 256 + c0), lv);
     }
+    tmem_st_wait();
   }
-  tc_teardown(tmem, 128);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if ((threadIdx.x >> 5) == 0) tmem_free(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -378,7 +429,7 @@ cudaError_t prep(K kern, size_t smem) {
 }
 constexpr size_t kRing3 = 2 * 3 * (size_t)SLICE_BYTES;   // 192 KB
 constexpr size_t kRing2 = 2 * 2 * (size_t)SLICE_BYTES;   // 128 KB
-constexpr size_t kScan = 6 * (size_t)SLICE_BYTES;        // state tile + ring, 192 KB
+constexpr size_t kScan = (kScanSlots + 4) * (size_t)kScanSliceBytes;   // raw ring + lo, 224 KB
 }  // namespace
 
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,

@@ -41,7 +41,9 @@ struct Workspace {
   float* pdb;    // [C][D]  partial db  (B3)
   float* pdgc;   // [C][D]  partial dgc (B3)
   // affine form of the state recurrence (tensor-core path)
-  float* M;      // [D][D]  diag(e^{gc_last}) - kg^T W
+  float* M;      // [2][D][D] M = diag(e^{gc_last}) - kg^T W as scan operands:
+                 //   [0, D^2): M as 4 K-slices, canonical 128 x 32 tiles (rows =
+                 //   row of M, K = column); [D^2, 2 D^2): the same for M^T
   float* Bc;     // [D][D]  kg^T U
   float* E;      // [D][D]  scale qg^T do - W^T dv_partial
   float* dvp;    // [C][D]  dv_partial = san(Aqk^T do)
@@ -51,7 +53,7 @@ struct Workspace {
   static size_t per_chunk_floats(int C, int D, bool bwd) {
     size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + D;   // forward
     f += (size_t)D * D + (size_t)C * D;                        // residuals
-    f += 2 * (size_t)D * D;                                    // M, Bc
+    f += 3 * (size_t)D * D;                                    // M (both ways), Bc
     if (bwd) f += 2 * (size_t)C * C + 7 * (size_t)C * D + 2 * (size_t)D * D;
     return f;
   }
@@ -76,7 +78,7 @@ struct Workspace {
     w.gcl = take((size_t)D);
     w.hpre = take((size_t)D * D);
     w.vnew = take((size_t)C * D);
-    w.M = take((size_t)D * D);
+    w.M = take(2 * (size_t)D * D);
     w.Bc = take((size_t)D * D);
     if (bwd) {
       w.dv = take((size_t)C * D);

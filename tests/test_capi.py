@@ -32,7 +32,7 @@ def test_workspace_bytes():
     lib = _lib.load()
     B, T, H, D, C = 8, 8192, 6, 128, 128
     nc = T // C
-    fwd = (2 * C * C + 5 * C * D + D + 3 * D * D + C * D) * 4 * B * H * nc + 512
+    fwd = (2 * C * C + 5 * C * D + D + 4 * D * D + C * D) * 4 * B * H * nc + 512
     bwd = fwd + (2 * C * C + 7 * C * D + 2 * D * D) * 4 * B * H * nc
     assert lib.gdn2_workspace_bytes(B, T, H, D, C, 0) == fwd
     assert lib.gdn2_workspace_bytes(B, T, H, D, C, 1) == bwd
