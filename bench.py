@@ -39,7 +39,7 @@ def flops_per_chunk(C, D):
         "fwd_intra": 4 * C * C * D + C ** 3 / 3,        # Aqk, Akk, (I+Akk)^-1, W, U
         "fwd_state": 6 * C * D * D + C * C * D,          # W h, qg h, kg^T vnew, Aqk vnew
         "bwd_state": 6 * C * D * D + C * C * D,          # kg dh, qg^T do, W^T dv, Aqk^T do
-        "bwd_intra1": 6 * C * D * D + C * C * D,         # dqg, dWp, dkg, dAqk
+        "bwd_intra1": 8 * C * D * D + C * C * D,         # dv_new, dqg, dWp, dkg, dAqk
         "bwd_intra2": 6 * C * C * D + 4 * C ** 3 / 3,    # dA (2), dkb, dwv, dA A^T, A^T tmp
         "bwd_intra3": 4 * C * C * D,                     # four pair-sum products of B4
         "fwd_affine": 4 * C * D * D,                     # kg^T W, kg^T U
@@ -47,7 +47,6 @@ def flops_per_chunk(C, D):
         "fwd_out": 4 * C * D * D + C * C * D,            # W h, qg h, Aqk vnew
         "bwd_prep": 4 * C * D * D + C * C * D,           # Aqk^T do, qg^T do, W^T dvp
         "bwd_scan": 2 * D ** 3,                          # M^T dh (serial)
-        "bwd_dvn": 2 * C * D * D,                        # kg dh_next
     }
 
 
@@ -59,21 +58,20 @@ def bytes_per_chunk(C, D):
         "fwd_intra": 6 * t + 2 * cc + 5 * t,
         "fwd_state": 4 * t + cc + 2 * t + s,
         "bwd_state": t + cc + 3 * t + t + s,
-        "bwd_intra1": 2 * t + 3 * t + 2 * s + 3 * t + cc,
-        "bwd_intra2": 5 * t + 2 * cc + t + 3 * t + 2 * t + cc,
+        "bwd_intra1": 2 * t + 3 * t + 2 * s + 3 * t + cc + 2 * t,   # + kg, dvp in, dv out, - dv in
+        "bwd_intra2": 13 * t + 2 * cc,   # A, dAkk^T; dWp, dv, k, b, gc, w, v, pdk, pdgc in; pdk, pdb, pdgc, dw, dv out
         "bwd_intra3": 4 * t + 2 * cc + 5 * t + 4 * t,
         "fwd_affine": 3 * t + 2 * s,
         "fwd_scan": 3 * s,
         "fwd_out": 3 * t + s + cc + 3 * t,
         "bwd_prep": cc + 3 * t + t + s,
         "bwd_scan": 3 * s,
-        "bwd_dvn": 3 * t + s,
     }
 
 
 # DRAM bytes (read + write) per chunk from one ncu capture of config 1 at B=1
 # (384 chunks; traffic grows with the chunk count), profiles/tc_intra_kernels_config1_b1.md.
-NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 778_091, "bwd_intra2": 1_239_323, "bwd_intra3": 972_301}
+NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 747_089, "bwd_intra2": 1_210_315, "bwd_intra3": 965_723}
 
 
 class ClockSampler:

@@ -66,9 +66,11 @@ __device__ __forceinline__ float4 exp4(float4 v) {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// dqg = scale do h_pre^T, dWp = -dv h_pre^T, dkg = vnew dh_next^T,
+// dv = san(dv_partial + kg dh_next) (B1's dv_new, gdn2_bwd.py:66-68, -> ws.dv),
+// then dqg = scale do h_pre^T, dWp = -dv h_pre^T, dkg = vnew dh_next^T,
 // dAqk = san((do vnew^T) * causal); writes pdq, pdk, pdgc (+ gc_last row),
-// dWp and dAqk^T exactly as k_bwd_intra1.
+// dWp and dAqk^T exactly as k_bwd_intra1.  dv stays in TMEM as the A operand
+// of dWp.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -92,16 +94,52 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   float *pdq = ws.pdq + chunk * C * D, *pdk = ws.pdk + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
   const uint32_t tmem = setup(&ts);
-  Ring ring = ring_of(sm, &ts, 3);
+  Ring ring = ring_of(sm, &ts, 2);
   int g = 0;
-  // contraction over the value dim v for every product
+  uint32_t ph = 0;
+  // dv = san(dvp + kg dh_next)  (TMEM 0, contraction over d)
   {
-    const Src srcs[3] = {direct(doc, rs), direct(dvn, D, -1.f), direct(hpre, D)};  // (i,v) (i,v) (dk,v)
+    const Src srcs[2] = {direct(ws.kg + chunk * C * D, D), trans(dhn, D)};   // (i,d), (v,d)
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
     });
   }
+  drain(&ts.done, ph, ws.status);
+  {
+    const float* dvp = ws.dvp + chunk * C * D;
+    float* dv = ws.dv + chunk * C * D;
+    for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
+      float hv[16], lv[16];
+#pragma unroll
+      for (int k = 0; k < 16; k += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(dvp + i * D + c0 + k);
+        const float4 y = make_float4(san(a.x + x[k], p.clip), san(a.y + x[k + 1], p.clip),
+                                     san(a.z + x[k + 2], p.clip), san(a.w + x[k + 3], p.clip));
+        *reinterpret_cast<float4*>(dv + i * D + c0 + k) = y;
+        split(-y.x, hv[k], lv[k]);
+        split(-y.y, hv[k + 1], lv[k + 1]);
+        split(-y.z, hv[k + 2], lv[k + 2]);
+        split(-y.w, hv[k + 3], lv[k + 3]);
+      }
+      tmem_st16(lane_quarter_addr(tmem, 256 + c0), hv);   // -dv: A operand (rows i, K = v)
+      tmem_st16(lane_quarter_addr(tmem, 384 + c0), lv);
+    });
+    tmem_st_wait();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  // contraction over the value dim v for every product
+  {
+    const Src srcs[2] = {direct(doc, rs), direct(hpre, D)};  // (i,v) (dk,v)
+    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
+      mma3_ta(tmem + 128, tmem + 256 + s * KS, tmem + 384 + s * KS, ring.op(buf, 1), 128, KS / 8,
+              s > 0);
+    });
+  }
+  drain(&ts.done, ph, ws.status);   // TMEM 256..511 free again
+  ring.nop = 3;
   {
     const Src srcs[3] = {direct(vnew, D), direct(doc, rs), direct(dhn, D)};  // (i|j,v) (i,v) (dk,v)
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
@@ -109,7 +147,6 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
       mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);
     });
   }
-  uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
   float* t0 = sm;                  // the ring is free: two padded 128 x 128 tiles
   float* t1 = sm + TILE_FLOATS;

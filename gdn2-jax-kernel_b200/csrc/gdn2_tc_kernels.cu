@@ -8,9 +8,9 @@
 //     E_c = scale qg^T do - W^T dv_partial,   dv_partial = san(Aqk^T do).
 // M_c, Bc_c and E_c are chunk-parallel products; the serial chain keeps one
 // 128 x 128 x 128 product per chunk.  The outputs o = scale qg h + Aqk vnew,
-// vnew = U - W h and dv_new = san(dv_partial + kg dh_next) are chunk-parallel
-// again.  Sanitisers sit where the reference has them (h and dh after every
-// chunk, o, dv_partial, dv_new).
+// vnew = U - W h and dv_new = san(dv_partial + kg dh_next) (formed in the
+// backward intra kernel) are chunk-parallel again.  Sanitisers sit where the
+// reference has them (h and dh after every chunk, o, dv_partial, dv_new).
 #include "gdn2_kernels.cuh"
 #include "gdn2_tc_stage.cuh"
 
@@ -387,39 +387,6 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   tc_teardown(tmem, 256);
 }
 
-// ---------------------------------------------------------------------------
-// dv_new = san(dv_partial + kg dh_next)  (gdn2_bwd.py:66-68)  -> ws.dv
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1)
-k_tc_bwd_dvn(Problem p, Workspace ws, const float* __restrict__ dh_final) {
-  extern __shared__ __align__(128) float sm[];
-  __shared__ TcSmem ts;
-  const size_t chunk = blockIdx.x;
-  const int c = (int)(chunk % p.nc);
-  const size_t bh = chunk / p.nc;
-  const uint32_t tmem = tc_setup(&ts, 128);
-  Ring ring = make_ring(sm, &ts, 2);
-  const float* kg = ws.kg + chunk * C * D;
-  const float* dhn = (c + 1 < p.nc) ? ws.dh + (chunk + 1) * D * D : dh_final + bh * D * D;
-  int g = 0;
-  const Src srcs[2] = {direct(kg, D), trans(dhn, D)};   // (i,d), (v,d)
-  kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
-  });
-  uint32_t ph = 0;
-  drain(&ts.done, ph, ws.status);
-  const float* dvp = ws.dvp + chunk * C * D;
-  float* dv = ws.dv + chunk * C * D;
-  for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
-#pragma unroll
-    for (int k = 0; k < 16; k += 4) {
-      const float4 a = ld4f(dvp + i * D + c0 + k);
-      st4f(dv + i * D + c0 + k, make_float4(san(a.x + x[k], p.clip), san(a.y + x[k + 1], p.clip),
-                                            san(a.z + x[k + 2], p.clip), san(a.w + x[k + 3], p.clip)));
-    }
-  });
-  tc_teardown(tmem, 128);
-}
 
 // ---------------------------------------------------------------------------
 namespace {
@@ -428,7 +395,6 @@ cudaError_t prep(K kern, size_t smem) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 constexpr size_t kRing3 = 2 * 3 * (size_t)SLICE_BYTES;   // 192 KB
-constexpr size_t kRing2 = 2 * 2 * (size_t)SLICE_BYTES;   // 128 KB
 constexpr size_t kScan = (kScanSlots + 4) * (size_t)kScanSliceBytes;   // raw ring + lo, 224 KB
 }  // namespace
 
@@ -461,7 +427,6 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
   const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
   if ((e = prep(k_tc_bwd_prep, kRing3)) != cudaSuccess) return e;
   if ((e = prep(k_tc_scan<true>, kScan)) != cudaSuccess) return e;
-  if ((e = prep(k_tc_bwd_dvn, kRing2)) != cudaSuccess) return e;
   hook.begin(kStageBwdPrep, s);
   k_tc_bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, dout);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -470,10 +435,7 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
   k_tc_scan<true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, dh_final, dh0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdScan, s);
-  hook.begin(kStageBwdDvn, s);
-  k_tc_bwd_dvn<<<nchunks, kThreads, kRing2, s>>>(p, ws, dh_final);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  hook.end(kStageBwdDvn, s);
+  // dv_new is formed by the first product of k_tc_bwd_intra1
   return cudaSuccess;
 }
 
