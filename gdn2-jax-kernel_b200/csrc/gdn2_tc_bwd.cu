@@ -397,7 +397,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const long rs = p.row_stride();
   const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
   const T *qc = q + off, *kc = k + off, *bc = b + off, *gcp = g + off;
-  const float* gc = ws.gc + chunk * C * D;
+  const float* gcg = ws.gc + chunk * C * D;
   const float* pdq = ws.pdq + chunk * C * D;
   const float* pdk = ws.pdk + chunk * C * D;
   const float* pdb = ws.pdb + chunk * C * D;
@@ -408,6 +408,14 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   float* sdg = sm;   // [C][D] after the products (ring area)
 
   const uint32_t tmem = setup(&ts);
+  // gc tile resident in shared memory after the ring: read by every operand
+  // staging and epilogue below
+  float* sgc = sm + 2 * 2 * 2 * SLICE_FLOATS;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < C * D / 4; e += kThreads)
+    *reinterpret_cast<float4*>(sgc + 4 * e) = *reinterpret_cast<const float4*>(gcg + 4 * e);
+  __syncthreads();
+  const float* gc = sgc;
   float gpos = -1.f;
 #pragma unroll 8
   for (int it = 0; it < C * D / 4 / kThreads; ++it) {
@@ -633,8 +641,8 @@ template <typename T>
 cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g, T* dq, T* dk,
                                  T* db, T* dg, const Problem& p, const Workspace& ws,
                                  cudaStream_t s, const LaunchHook& hook) {
-  constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES;   // ring; also holds the C x D dgc tile
-  static_assert(smem >= (size_t)C * D * sizeof(float), "dgc tile fits");
+  // ring (also the C x D dgc tile at the end), then the gc tile
+  constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES + (size_t)C * D * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k_tc_bwd_intra3<T>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
