@@ -28,6 +28,14 @@ BT = 256     # chunk length
 BC = 128     # sub-block length (the reference's clip granularity; results do not depend on it)
 MB = 16      # micro-block of the triangular solve
 CLIP = 1e4   # stage sanitiser bound
+# Chunk length policy.  EXACT_BT = True (default) runs chunks of BT itself
+# (split into 128 or 64 when BT is larger), which reproduces the reference
+# bit for bit in where its clips act.  EXACT_BT = False lets a head dim of
+# 128 run chunks of 128 (the tensor-core kernels) whenever T allows, whatever
+# BT says: the chunked form is exact for any chunk length, so results agree
+# to float32 rounding unless a gate is positive and the +-20 exponent clip or
+# CLIP saturate (they act per chunk).
+EXACT_BT = True
 
 _GDN2_FWD_DIAG = os.environ.get("GDN2_FWD_DIAG", "0") == "1"
 _KERNEL_CHUNKS = (128, 64)
@@ -39,12 +47,16 @@ class Gdn2ShapeError(ValueError, AssertionError):
     the reference rejects these with ``assert`` (gdn2_fwd.py:145-146)."""
 
 
-def _kernel_chunk(T, bt):
+def _kernel_chunk(T, bt, D):
     """Chunk length the kernels run with for the user's BT.  The chunked form
-    is exact for any chunk length (only the +-20 pair-decay clip and CLIP see
-    the chunking), so a BT of 256 runs as chunks of 128 when T allows it."""
+    is exact for any chunk length: only the +-20 pair-decay clip and CLIP see
+    the chunking, and both act on saturated inputs alone.  So a BT of 256 runs
+    as chunks of 128, and with EXACT_BT = False a head dim of 128 runs chunks
+    of 128 for any BT that divides T (the tensor-core path)."""
     if T % bt != 0:
         raise Gdn2ShapeError(f"L={T} must be divisible by BT={bt}.")
+    if not EXACT_BT and D == 128 and T % 128 == 0:
+        return 128
     for c in _KERNEL_CHUNKS:
         if bt % c == 0 and T % c == 0 and c <= bt:
             return c
@@ -83,7 +95,7 @@ class _Prepared:
             raise Gdn2ShapeError(f"head dim D={D} unsupported (64 or 128)")
         self.B, self.T, self.H, self.D = B, T, H, D
         self.bt_user = int(BT)
-        self.C = _kernel_chunk(T, self.bt_user)
+        self.C = _kernel_chunk(T, self.bt_user, D)
         bc = int(BC)
         if bc <= 0 or self.bt_user % bc != 0:
             raise Gdn2ShapeError(f"BC={bc} must divide BT={self.bt_user}")

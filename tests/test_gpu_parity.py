@@ -77,6 +77,28 @@ def test_forward_backward_vs_oracle(B, T, H, D, BT, BC, h0s, dtype):
         assert rel(a, b) < tol, (name, rel(a, b))
 
 
+@pytest.mark.parametrize("exact", [False, True])
+def test_bt64_chunking_policy(exact):
+    """BT=64 with D=128: by default the kernels run 128-row chunks (tensor
+    cores); EXACT_BT runs 64-row chunks (CUDA cores).  Both match the oracle
+    run at BT=64, and each other to float32 rounding."""
+    from gdn2_package import gdn2_fwd
+    _set_consts(64, 16, 1e4)
+    gdn2_fwd.EXACT_BT = exact
+    inp = make_inputs(2, 512, 2, 128, seed=21, h0_std=0.1)
+    args = _dev(inp, torch.float32)
+    h0 = torch.as_tensor(inp["h0"]).cuda()
+    o, h = gdn2_pallas_forward(*args, inp["scale"], h0)
+    ref_in = _rounded(inp, torch.float32)
+    o_r, h_r = O.forward(*ref_in, inp["scale"], inp["h0"], 64, 16, 1e4)
+    assert rel(o, o_r) < 1e-5 and rel(h, h_r) < 1e-5, (rel(o, o_r), rel(h, h_r))
+    grads = gdn2_backward(*args, inp["scale"], h0, torch.as_tensor(inp["dout"]).cuda(),
+                          torch.as_tensor(inp["dh_final"]).cuda())
+    g_r = O.backward(*ref_in, inp["scale"], inp["h0"], inp["dout"], inp["dh_final"], 64, 16, 1e4)
+    for name, a, b in zip(GRADS, grads, g_r):
+        assert rel(a, b) < 1e-5, (name, rel(a, b))
+
+
 @pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64"])
 def test_against_reference_golden(name):
     """Outputs of the reference source itself (tests/golden/make_golden.py)."""

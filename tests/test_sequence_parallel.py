@@ -61,7 +61,7 @@ starts, final = SP.compose_forward(maps, consts, torch.zeros(shape))
 ref_s, ref_f = SP.compose_forward(allP, allc, torch.zeros(shape))
 assert all(torch.allclose(a, b) for a, b in zip(starts, ref_s)) and torch.allclose(final, ref_f)
 dist.destroy_process_group()
-print("ok", r)
+open(os.path.join(sys.argv[2], f"ok{r}"), "w").close()   # one marker file per rank
 '''
 
 
@@ -69,10 +69,11 @@ def test_exchange_over_gloo_two_ranks(tmp_path):
     script = tmp_path / "w.py"
     script.write_text(_GLOO_WORKER)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29533", str(script), ROOT]
+           "--master-addr", "127.0.0.1", "--master-port", "29533", str(script), ROOT,
+           str(tmp_path)]
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=240)
     assert out.returncode == 0, out.stderr[-2000:]
-    assert "ok 0" in out.stdout and "ok 1" in out.stdout
+    assert (tmp_path / "ok0").exists() and (tmp_path / "ok1").exists()
 
 
 def _inputs(B, T, H, seed):
