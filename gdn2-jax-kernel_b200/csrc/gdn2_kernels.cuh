@@ -108,6 +108,64 @@ __device__ __forceinline__ void column_cumsum(float* s, float* tot) {
   __syncthreads();
 }
 
+// One doubling level of wy_inverse_T128 (blocks of 2*HALF, A10 = -A11 (T10
+// A00)) on register tiles: each block's HALF x HALF outputs go to
+// HALF*HALF/(TM*TN) threads with TM x TN outputs each.  The sums run over the
+// full K range; the operands' upper-triangle entries are exact zeros in S, so
+// the result equals the triangular sums bit for bit.
+template <int HALF, int TM, int TN>
+__device__ __forceinline__ void wy_level_tiled(float* S, int ld, float* tmp, float clip) {
+  constexpr int P = HALF * HALF / (TM * TN);      // threads per block
+  constexpr int TX = HALF / TN;
+  static_assert(P * (128 / (2 * HALF)) == kThreads, "one pass over the blocks");
+  const int beta = threadIdx.x / P, u = threadIdx.x % P;
+  const int i0 = (u / TX) * TM, j0 = (u % TX) * TN, o = beta * 2 * HALF;
+  float* tb = tmp + beta * HALF * HALF;           // tb[j * HALF + i] = tmp(i, j)
+  float acc[TM][TN];
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TN; ++b) acc[a][b] = 0.f;
+#pragma unroll 4
+  for (int kk = 0; kk < HALF; ++kk) {             // tmp = T10 A00
+    float av[TM], bv[TN];
+#pragma unroll
+    for (int a = 0; a < TM; ++a) av[a] = S[(o + kk) * ld + o + HALF + i0 + a];
+#pragma unroll
+    for (int b = 0; b < TN; ++b) bv[b] = S[(o + j0 + b) * ld + o + kk];
+#pragma unroll
+    for (int a = 0; a < TM; ++a)
+#pragma unroll
+      for (int b = 0; b < TN; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TN; ++b) tb[(j0 + b) * HALF + i0 + a] = san(acc[a][b], clip);
+  __syncthreads();
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TN; ++b) acc[a][b] = 0.f;
+#pragma unroll 4
+  for (int kk = 0; kk < HALF; ++kk) {             // A10 = -A11 tmp
+    float av[TM], bv[TN];
+#pragma unroll
+    for (int a = 0; a < TM; ++a) av[a] = S[(o + HALF + kk) * ld + o + HALF + i0 + a];
+#pragma unroll
+    for (int b = 0; b < TN; ++b) bv[b] = tb[(j0 + b) * HALF + kk];
+#pragma unroll
+    for (int a = 0; a < TM; ++a)
+#pragma unroll
+      for (int b = 0; b < TN; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TN; ++b) S[(o + j0 + b) * ld + o + HALF + i0 + a] = san(-acc[a][b], clip);
+  __syncthreads();
+}
+
 // wy_inverse_T for C = 128 with the last doubling level (two 64 x 64 x 64
 // products) on register tiles.  `tmp` needs 4096 floats, `scr` 2 * 64 * 68.
 __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr,
@@ -129,28 +187,8 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
     for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
   }
   __syncthreads();
-#pragma unroll 1
-  for (int s = 2 * MBK; s < C; s *= 2) {
-    const int half = s / 2, per = half * half, total = (C / s) * per;
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
-      const int o = beta * s;
-      float acc = 0.f;
-      for (int kk = j; kk < half; ++kk)
-        acc = fmaf(S[(o + kk) * ld + o + half + i], S[(o + j) * ld + o + kk], acc);
-      tmp[beta * per + j * half + i] = san(acc, clip);
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
-      const int o = beta * s;
-      float acc = 0.f;
-      for (int kk = 0; kk <= i; ++kk)
-        acc = fmaf(S[(o + half + kk) * ld + o + half + i], tmp[beta * per + j * half + kk], acc);
-      S[(o + j) * ld + o + half + i] = san(-acc, clip);
-    }
-    __syncthreads();
-  }
+  wy_level_tiled<16, 2, 2>(S, ld, tmp, clip);   // blocks of 32
+  wy_level_tiled<32, 2, 4>(S, ld, tmp, clip);   // blocks of 64
   // last level: T10 = M(64.., 0..63), A00 = A(0..63, 0..63), A11 = A(64.., 64..)
   float* y = scr;             // y[k][j] = A00(k, j)   (row-major copy)
   float* t = scr + H * LY;    // t[k][j] = tmp(k, j)
