@@ -16,6 +16,7 @@ constexpr float kFinalClipTc = 1e4f;   // gdn2_pipeline.py:34
 
 struct TcSmemB {
   float colpart[8][D];   // first member: 16-byte aligned for float4 stores
+  float rowdot[D];
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
@@ -194,12 +195,26 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     const int d = (threadIdx.x & 31) * 4;
     st4(&ts.colpart[threadIdx.x >> 5][d], cs[0], cs[1], cs[2], cs[3]);
   }
+  // rowdot[d] = sum_v dh_next(d, v) h_pre(d, v): one warp per 16 rows, a lane
+  // per 4 columns, fixed-order shuffle reduction
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 4
+    for (int rr = 0; rr < D / 8; ++rr) {
+      const int d = warp * (D / 8) + rr;
+      const float4 a = *reinterpret_cast<const float4*>(dhn + d * D + lane * 4);
+      const float4 h4 = *reinterpret_cast<const float4*>(hpre + d * D + lane * 4);
+      float v = a.x * h4.x + a.y * h4.y + a.z * h4.z + a.w * h4.w;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) ts.rowdot[d] = v;
+    }
+  }
   __syncthreads();
   // gc_last row: sum_i dkg kg + e^{gc_last} sum_v dh_next h_pre (gdn2_bwd.py:185, 196-201)
   if (threadIdx.x < D) {
     const int d = threadIdx.x;
-    float sdot = 0.f;
-    for (int vv = 0; vv < D; ++vv) sdot = fmaf(dhn[d * D + vv], hpre[d * D + vv], sdot);
+    const float sdot = ts.rowdot[d];
     float csum = 0.f;
     for (int r = 0; r < 8; ++r) csum += ts.colpart[r][d];   // fixed order
     pdgc[(C - 1) * D + d] += csum + __expf(gl[d]) * sdot;
