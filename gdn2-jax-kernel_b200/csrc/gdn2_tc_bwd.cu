@@ -299,17 +299,50 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   {
     ring.base = sm;
     ring.nop = 2;
+    // the computed operands (kb, then wv) are loaded a slice ahead in
+    // registers, in the thread -> (row, column) map of store_direct
+    auto rc = [&](int it, int& r, int& cc) {
+      const int e = threadIdx.x + it * kThreads, lane = e & 31, w = e >> 5;
+      r = (w & 15) * 8 + (lane & 7);
+      cc = ((w >> 4) * 4 + (lane >> 3)) * 4;
+    };
+    Frag fx, fy, fz;
+    auto ld_kb = [&](int sl) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        int j, cc;
+        rc(it, j, cc);
+        const int d = sl * KS + cc;
+        fx.v[it] = ld4<T>(kc + j * rs + d);
+        fy.v[it] = ld4<T>(bc + j * rs + d);
+        fz.v[it] = ldg4(gc + j * D + d);
+      }
+    };
+    auto ld_wv = [&](int sl) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        int j, cc;
+        rc(it, j, cc);
+        const int d = sl * KS + cc;
+        fx.v[it] = ld4<T>(wc + j * rs + d);
+        fy.v[it] = ld4<T>(vc + j * rs + d);
+      }
+    };
+    ld_kb(0);
     {
       const Src srcs[1] = {direct(dwp, D)};   // (i,d)
       kloop_pf(ring, g, ws.status, srcs,
                [&](int buf, int s) {
-                 stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) kb
-                   const int d = s * KS + cc;
-                   const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
-                   const float4 g4 = ldg4(gc + j * D + d);
-                   return make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
-                                      bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
-                 });
+                 Frag kb;   // (j,d) = b k e^gc
+#pragma unroll
+                 for (int it = 0; it < 4; ++it) {
+                   const float4 kv = fx.v[it], bv = fy.v[it], g4 = fz.v[it];
+                   kb.v[it] = make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
+                                          bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
+                 }
+                 if (s + 1 < D / KS) ld_kb(s + 1);
+                 else ld_wv(0);
+                 store_direct(ring.hi(buf, 1), ring.lo(buf, 1), kb);
                },
                [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0); });
     }
@@ -317,11 +350,14 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
       const Src srcs[1] = {direct(dvn, D)};   // (i,d)
       kloop_pf(ring, g, ws.status, srcs,
                [&](int buf, int s) {
-                 stage_direct_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int j, int cc) {   // (j,d) wv
-                   const int d = s * KS + cc;
-                   const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
-                   return make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
-                 });
+                 Frag wv;   // (j,d) = w v
+#pragma unroll
+                 for (int it = 0; it < 4; ++it) {
+                   const float4 a = fx.v[it], b4 = fy.v[it];
+                   wv.v[it] = make_float4(a.x * b4.x, a.y * b4.y, a.z * b4.z, a.w * b4.w);
+                 }
+                 if (s + 1 < D / KS) ld_wv(s + 1);
+                 store_direct(ring.hi(buf, 1), ring.lo(buf, 1), wv);
                },
                [&](int buf, int s) { mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1); });
     }
