@@ -116,10 +116,10 @@ __device__ __forceinline__ void column_cumsum(float* s, float* tot) {
 template <int HALF, int TM, int TN>
 __device__ __forceinline__ void wy_level_tiled(float* S, int ld, float* tmp, float clip) {
   constexpr int P = HALF * HALF / (TM * TN);      // threads per block
-  constexpr int TX = HALF / TN;
+  constexpr int TXI = HALF / TM;                  // lanes along i: contiguous rows
   static_assert(P * (128 / (2 * HALF)) == kThreads, "one pass over the blocks");
   const int beta = threadIdx.x / P, u = threadIdx.x % P;
-  const int i0 = (u / TX) * TM, j0 = (u % TX) * TN, o = beta * 2 * HALF;
+  const int i0 = (u % TXI) * TM, j0 = (u / TXI) * TN, o = beta * 2 * HALF;
   float* tb = tmp + beta * HALF * HALF;           // tb[j * HALF + i] = tmp(i, j)
   float acc[TM][TN];
 #pragma unroll

@@ -461,10 +461,13 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const uint32_t tmem = setup(&ts);
   // gc tile resident in shared memory after the ring: read by every operand
   // staging and epilogue below
+  // (row stride GLD: per-row reads of consecutive rows hit distinct banks)
+  constexpr int GLD = D + 4;
   float* sgc = sm + 2 * 2 * 2 * SLICE_FLOATS;
 #pragma unroll 4
   for (int e = threadIdx.x; e < C * D / 4; e += kThreads)
-    *reinterpret_cast<float4*>(sgc + 4 * e) = *reinterpret_cast<const float4*>(gcg + 4 * e);
+    *reinterpret_cast<float4*>(sgc + (e >> 5) * GLD + (e & 31) * 4) =
+        *reinterpret_cast<const float4*>(gcg + 4 * e);
   __syncthreads();
   const float* gc = sgc;
   float gpos = -1.f;
@@ -478,8 +481,8 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   float spread = 0.f, spread64 = 0.f;
   for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
     const int J = e / D, d = e % D;
-    spread = fmaxf(spread, fabsf(gc[(32 * J) * D + d] - gc[(32 * J + 31) * D + d]));
-    if (J < 2) spread64 = fmaxf(spread64, fabsf(gc[(64 * J) * D + d] - gc[(64 * J + 63) * D + d]));
+    spread = fmaxf(spread, fabsf(gc[(32 * J) * GLD + d] - gc[(32 * J + 31) * GLD + d]));
+    if (J < 2) spread64 = fmaxf(spread64, fabsf(gc[(64 * J) * GLD + d] - gc[(64 * J + 63) * GLD + d]));
   }
   const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
   const int JW = block_max(spread64, red) <= 80.f ? 64 : 32;
@@ -507,7 +510,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, jj) = R
             const int j = k0 + kk;
             const float4 kv = ld4<T>(kc + j * rs + d);
-            const float4 gj = ldg4(gc + j * D + d), gr = ldg4(gc + r * D + d);
+            const float4 gj = ldg4(gc + j * GLD + d), gr = ldg4(gc + r * GLD + d);
             return make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
                                kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w));
           });
@@ -515,7 +518,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, k0, Ident{});  // (j, ii) = dM(k0+ii, j)
           stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, ii) = L
             const int i = k0 + kk;
-            const float4 gi = ldg4(gc + i * D + d), gr = ldg4(gc + r * D + d);
+            const float4 gi = ldg4(gc + i * GLD + d), gr = ldg4(gc + r * GLD + d);
             float4 lv;
             if (pass == 2) {
               const float4 qv = ld4<T>(qc + i * rs + d);
@@ -544,7 +547,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         float gx[16];
 #pragma unroll
         for (int t = 0; t < 16; t += 4) {
-          const float4 v4 = ldg4(gc + x * D + c0 + t);
+          const float4 v4 = ldg4(gc + x * GLD + c0 + t);
           gx[t] = v4.x; gx[t + 1] = v4.y; gx[t + 2] = v4.z; gx[t + 3] = v4.w;
         }
 #pragma unroll
@@ -557,7 +560,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           if (use) {
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
-              const float gr = gc[r * D + c0 + t];
+              const float gr = gc[r * GLD + c0 + t];
               val[t] += a[t] * __expf(left ? gx[t] - gr : gr - gx[t]);
             }
           }
@@ -650,7 +653,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       float dlq = 0.f, dlk = 0.f, drq = 0.f, drk = 0.f, dgi = 0.f, dgj = 0.f;
       for (int y = 0; y < C; ++y) {
         if (y <= x) {
-          const float dd = gc[x * D + d] - gc[y * D + d];
+          const float dd = gc[x * GLD + d] - gc[y * GLD + d];
           const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
           const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
           const float mq = dAqkT[y * C + x], mk = (y < x) ? dAkkT[y * C + x] : 0.f;
@@ -660,7 +663,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           dgi += (mq * lq + mk * lk) * ry * cm;
         }
         if (y >= x) {
-          const float dd = gc[y * D + d] - gc[x * D + d];
+          const float dd = gc[y * GLD + d] - gc[x * GLD + d];
           const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
           const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
           const float mq = dAqkT[x * C + y], mk = (y > x) ? dAkkT[x * C + y] : 0.f;
@@ -693,7 +696,7 @@ cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g,
                                  T* db, T* dg, const Problem& p, const Workspace& ws,
                                  cudaStream_t s, const LaunchHook& hook) {
   // ring (also the C x D dgc tile at the end), then the gc tile
-  constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES + (size_t)C * D * sizeof(float);
+  constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES + (size_t)C * (D + 4) * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k_tc_bwd_intra3<T>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
