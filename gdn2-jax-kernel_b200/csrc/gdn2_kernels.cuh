@@ -88,22 +88,22 @@ __device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, float
 
 // Column-wise inclusive prefix sum of a C x D tile held row-major in shared
 // memory (ld = D).  256 threads: each column split into 256/D row segments.
-template <int C, int D>
+template <int C, int D, int LD = D>
 __device__ __forceinline__ void column_cumsum(float* s, float* tot) {
   constexpr int NSEG = kThreads / D;
   constexpr int RS = C / NSEG;
   const int d = threadIdx.x % D, seg = threadIdx.x / D;
   float acc = 0.f;
 #pragma unroll 8
-  for (int r = seg * RS; r < (seg + 1) * RS; ++r) acc += s[r * D + d];
+  for (int r = seg * RS; r < (seg + 1) * RS; ++r) acc += s[r * LD + d];
   tot[seg * D + d] = acc;
   __syncthreads();
   float off = 0.f;
   for (int sg = 0; sg < seg; ++sg) off += tot[sg * D + d];
 #pragma unroll 8
   for (int r = seg * RS; r < (seg + 1) * RS; ++r) {
-    off += s[r * D + d];
-    s[r * D + d] = off;
+    off += s[r * LD + d];
+    s[r * LD + d] = off;
   }
   __syncthreads();
 }

@@ -33,6 +33,7 @@ using namespace tc;
 namespace {
 
 constexpr int C = 128, D = 128;
+constexpr int GLD = D + 4;   // row stride of the resident gc tile (conflict-free row reads)
 // threads issuing MMAs: lane 0 of warps 0 .. kIss-1, one accumulator each
 #ifndef GDN2_FWD_ISS
 #define GDN2_FWD_ISS 2
@@ -40,7 +41,6 @@ constexpr int C = 128, D = 128;
 constexpr int kIss = GDN2_FWD_ISS;
 
 struct TcSmemF {
-  float red[264];
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
@@ -69,13 +69,14 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
   const T *qc = q + off, *kc = k + off, *vc = v + off, *wc = w + off, *bc = b + off,
           *gcp = g + off;
-  // shared memory plan (floats): gc stays in [0, 16384) through phase 3; the
+  // shared memory plan (floats): gc stays in [0, C * GLD) through phase 3; the
   // score ring, then the transposed score tiles and the solve, follow it;
   // phase 3 puts its ring after gc (A itself moves to TMEM).
-  float* sgc = sm;
-  float* ringA = sm + C * D;                       // 2 buffers x 2 operands x slice
+  float* sgc = sm;                                 // [C][GLD]
+  float* red = sm + C * GLD;                       // phase-0 reduction scratch (256 floats)
+  float* ringA = sm + C * GLD;                     // 2 buffers x 2 operands x slice
   float* bsl = ringA + 2 * 2 * 2 * SLICE_FLOATS;   // 2 buffers x (hi, lo) x 64 x 32
-  float* t0 = sm + C * D;                          // after the score products
+  float* t0 = sm + C * GLD;                        // after the score products
   float* S = t0 + TILE_FLOATS;
   float* tmp = S + TILE_FLOATS;                    // 4096 floats
 
@@ -93,44 +94,45 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   for (int it = 0; it < C * D / 4 / kThreads; ++it) {
     const int e = threadIdx.x + it * kThreads;
     const int r = e >> 5, cc = (e & 31) * 4;
-    sts4(sgc + r * D + cc, ld4<T>(gcp + r * rs + cc));
+    sts4(sgc + r * GLD + cc, ld4<T>(gcp + r * rs + cc));
   }
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = ts.tmem;
   float gpos = -1.f;
-  for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[e]);
-  const float gmax = block_max(gpos, ts.red);
-  column_cumsum<C, D>(sgc, ts.red);
+  for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[(e / D) * GLD + e % D]);
+  const float gmax = block_max(gpos, red);
+  column_cumsum<C, D, GLD>(sgc, red);
   // largest decay-block width (64 or 32 rows) whose in-block gc spread keeps
   // every factor e^{gc_r - gc_j} inside the float range
   float spread = 0.f, spread64 = 0.f;
   for (int e = threadIdx.x; e < 4 * D; e += kThreads) {
     const int J = e / D, d = e % D;
-    spread = fmaxf(spread, fabsf(sgc[(32 * J) * D + d] - sgc[(32 * J + 31) * D + d]));
-    if (J < 2) spread64 = fmaxf(spread64, fabsf(sgc[(64 * J) * D + d] - sgc[(64 * J + 63) * D + d]));
+    spread = fmaxf(spread, fabsf(sgc[(32 * J) * GLD + d] - sgc[(32 * J + 31) * GLD + d]));
+    if (J < 2) spread64 = fmaxf(spread64, fabsf(sgc[(64 * J) * GLD + d] - sgc[(64 * J + 63) * GLD + d]));
   }
-  const bool exact = gmax > 0.f || block_max(spread, ts.red) > 80.f || spread != spread;
-  const int JW = block_max(spread64, ts.red) <= 80.f ? 64 : 32;
+  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
+  const int JW = block_max(spread64, red) <= 80.f ? 64 : 32;
   {
     float* gco = ws.gc + chunk * C * D;
-    for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4) sts4(gco + e, lds4(sgc + e));
-    if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * D + threadIdx.x], p.clip);
+    for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4)
+      sts4(gco + e, lds4(sgc + (e / D) * GLD + e % D));
+    if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * GLD + threadIdx.x], p.clip);
     float* kgo = ws.kg + chunk * C * D;
-    const float* gl = sgc + (C - 1) * D;
+    const float* gl = sgc + (C - 1) * GLD;
     // qg is staged transposed with an odd row stride; a warp covers 4 rows x 32
     // columns, so the transposed scalar stores hit 32 distinct banks and the
     // global rows are read in 128-byte pieces.
     constexpr int QLD = C + 1;
-    float* tq = sm + C * D;   // free until the score products start
+    float* tq = sm + C * GLD;   // free until the score products start
 #pragma unroll 4
     for (int it = 0; it < C * D / 4 / kThreads; ++it) {
       const int e = threadIdx.x + it * kThreads;
       const int l = e & 31, wq = e >> 5;
       const int i = (wq & 31) * 4 + (l >> 3), d = ((wq >> 5) * 8 + (l & 7)) * 4;
       const float4 kv = ld4<T>(kc + i * rs + d), qv = ld4<T>(qc + i * rs + d);
-      const float4 gi = lds4(sgc + i * D + d), l4 = lds4(gl + d);
+      const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(gl + d);
       sts4(kgo + i * D + d, make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
                                         san(kv.y * __expf(l4.y - gi.y), p.clip),
                                         san(kv.z * __expf(l4.z - gi.z), p.clip),
@@ -207,7 +209,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           const int d = s * KS + cc;
           float4 aq = make_float4(0.f, 0.f, 0.f, 0.f), ak = aq;
           if (i >= r) {
-            const float4 gi = lds4(sgc + i * D + d), gr = lds4(sgc + r * D + d);
+            const float4 gi = lds4(sgc + i * GLD + d), gr = lds4(sgc + r * GLD + d);
             const float e0 = __expf(gi.x - gr.x), e1 = __expf(gi.y - gr.y),
                         e2 = __expf(gi.z - gr.z), e3 = __expf(gi.w - gr.w);
             const float4 qv = qx[it], kv = kx[it], bv = bx[it];
@@ -223,7 +225,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           const int jj = jb + (t & 7) + 8 * ((t >> 5) & 3), cc = 4 * ((t >> 3) & 3) + 16 * (t >> 7);
           const int d = s * KS + cc;
           const int j = r + jj;
-          const float4 gj = lds4(sgc + j * D + d), gr = lds4(sgc + r * D + d);
+          const float4 gj = lds4(sgc + j * GLD + d), gr = lds4(sgc + r * GLD + d);
           const float4 kv = ld4<T>(kc + j * rs + d);
           st_split4(bhi, blo, jj, cc, KS,
                     make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
@@ -260,7 +262,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       float sq = 0.f, sk = 0.f;
       if (j <= i) {
         for (int d = 0; d < D; ++d) {
-          const float ed = __expf(fminf(fmaxf(sgc[i * D + d] - sgc[j * D + d], -20.f), 20.f));
+          const float ed = __expf(fminf(fmaxf(sgc[i * GLD + d] - sgc[j * GLD + d], -20.f), 20.f));
           const float kj = to_f<T>(kc[j * rs + d]) * ed;
           sq = fmaf(to_f<T>(qc[i * rs + d]), kj, sq);
           sk = fmaf(to_f<T>(bc[i * rs + d]) * to_f<T>(kc[i * rs + d]), kj, sk);
@@ -299,7 +301,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 
   GDN2_TMARK(5);
   // ---- phase 3: W = A (b k e^gc), U = A (w v)  (gdn2_fwd.py:278-282)
-  ring.base = sm + C * D;   // after the gc tile
+  ring.base = sm + C * GLD;   // after the gc tile
   ring.nop = 2;
   {
     // b, k, w, v rows of the next slice are loaded while the current slice is
@@ -324,7 +326,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 #pragma unroll
                for (int jr = 0; jr < 4; ++jr) {
                  const int j = s * KS + kb4 * 4 + jr;
-                 const float4 bv = fb.v[jr], kv = fk.v[jr], g4 = lds4(sgc + j * D + rb * 4),
+                 const float4 bv = fb.v[jr], kv = fk.v[jr], g4 = lds4(sgc + j * GLD + rb * 4),
                               w4 = fw.v[jr], v4 = fv.v[jr];
                  kbf.v[jr] = make_float4(bv.x * kv.x * __expf(g4.x), bv.y * kv.y * __expf(g4.y),
                                          bv.z * kv.z * __expf(g4.z), bv.w * kv.w * __expf(g4.w));
@@ -370,12 +372,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 template <typename T>
 cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                                 const T* g, const Problem& p, const Workspace& ws, cudaStream_t s) {
-  constexpr size_t smem_rest = (size_t)(C * D + 2 * TILE_FLOATS + 4096) * sizeof(float);
-  constexpr size_t smem_scores = (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float);
+  constexpr size_t smem_rest = (size_t)(C * GLD + 2 * TILE_FLOATS + 4096) * sizeof(float);
+  constexpr size_t smem_scores = (size_t)(C * GLD + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float);
   constexpr size_t smem = smem_rest > smem_scores ? smem_rest : smem_scores;
-  static_assert(smem >= (size_t)(C * D + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float),
+  static_assert(smem >= (size_t)(C * GLD + 4 * SLICE_FLOATS * 2 + 4 * 64 * KS) * sizeof(float),
                 "score ring fits");
-  static_assert(smem >= (size_t)C * D * sizeof(float) + 2 * 2 * (size_t)SLICE_BYTES,
+  static_assert(smem >= (size_t)C * GLD * sizeof(float) + 2 * 2 * (size_t)SLICE_BYTES,
                 "phase-3 ring fits after the gc tile");
   cudaError_t e = cudaFuncSetAttribute(k_tc_fwd_intra<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
