@@ -151,45 +151,43 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   drain(&ts.done, ph, ws.status);
   float* t0 = sm;                  // the ring is free: two padded 128 x 128 tiles
   float* t1 = sm + TILE_FLOATS;
-  acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
-  acc_to_smem<false>(tmem, 128, t1);   // dWp
-  __syncthreads();
   float* dwp = ws.dWp + chunk * C * D;
+  for_acc<128>(tmem, 128, [&](int i, int c0, const float* x) {   // dWp straight out
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) st4(dwp + i * D + c0 + j, x[j], x[j + 1], x[j + 2], x[j + 3]);
+  });
+  acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
+  acc_to_smem<false>(tmem, 256, t1);   // dkg
+  __syncthreads();
+  // pdq = dqg e^gc; pdk = dkg e^{gc_last - gc}; pdgc = dqg q e^gc - dkg kg;
+  // column sums of dkg kg
+  const float* gl = gc + (C - 1) * D;
+  float cs[4] = {0.f, 0.f, 0.f, 0.f};
   for_tile([&](int i, int d) {
-    const float4 x = lds4(t0 + i * TLD + d);
-    const float4 eg = exp4(ldg4(gc + i * D + d));
-    const float4 qv = ld4<T>(qc + i * rs + d);
+    const float4 x = lds4(t0 + i * TLD + d), y = lds4(t1 + i * TLD + d);
+    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gl + d);
+    const float4 eg = exp4(g4);
+    const float4 qv = ld4<T>(qc + i * rs + d), kv = ld4<T>(kc + i * rs + d);
     const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
     st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
         san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
-    st4(pdgc + i * D + d, dqg.x * (qv.x * eg.x), dqg.y * (qv.y * eg.y), dqg.z * (qv.z * eg.z),
-        dqg.w * (qv.w * eg.w));
-    *reinterpret_cast<float4*>(dwp + i * D + d) = lds4(t1 + i * TLD + d);
+    const float4 pg = make_float4(dqg.x * (qv.x * eg.x), dqg.y * (qv.y * eg.y),
+                                  dqg.z * (qv.z * eg.z), dqg.w * (qv.w * eg.w));
+    const float4 f = exp4(make_float4(l4.x - g4.x, l4.y - g4.y, l4.z - g4.z, l4.w - g4.w));
+    const float4 xs = make_float4(y.x * (kv.x * f.x), y.y * (kv.y * f.y), y.z * (kv.z * f.z),
+                                  y.w * (kv.w * f.w));
+    st4(pdk + i * D + d, y.x * f.x, y.y * f.y, y.z * f.z, y.w * f.w);
+    st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
+    cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
   });
   __syncthreads();
   acc_to_smem<true>(tmem, 384, t0);    // t0[j][i] = dAqk(i, j)
-  acc_to_smem<false>(tmem, 256, t1);   // dkg
   __syncthreads();
   float* daqkT = ws.dAqkT + chunk * C * C;
   for_tile([&](int j, int i) {
     const float4 x = lds4(t0 + j * TLD + i);
     st4(daqkT + j * C + i, j <= i ? san(x.x, p.clip) : 0.f, j <= i + 1 ? san(x.y, p.clip) : 0.f,
         j <= i + 2 ? san(x.z, p.clip) : 0.f, j <= i + 3 ? san(x.w, p.clip) : 0.f);
-  });
-  // dkg -> pdk = dkg e^{gc_last - gc}; pdgc -= dkg kg; column sums of dkg kg
-  const float* gl = gc + (C - 1) * D;
-  float cs[4] = {0.f, 0.f, 0.f, 0.f};
-  for_tile([&](int i, int d) {
-    const float4 x = lds4(t1 + i * TLD + d);
-    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gl + d);
-    const float4 kv = ld4<T>(kc + i * rs + d);
-    const float4 f = exp4(make_float4(l4.x - g4.x, l4.y - g4.y, l4.z - g4.z, l4.w - g4.w));
-    const float4 xs = make_float4(x.x * (kv.x * f.x), x.y * (kv.y * f.y), x.z * (kv.z * f.z),
-                                  x.w * (kv.w * f.w));
-    st4(pdk + i * D + d, x.x * f.x, x.y * f.y, x.z * f.z, x.w * f.w);
-    const float4 pg = ldg4(pdgc + i * D + d);
-    st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
-    cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
   });
   {
     const int d = (threadIdx.x & 31) * 4;
