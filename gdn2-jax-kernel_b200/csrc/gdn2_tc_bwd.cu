@@ -280,12 +280,11 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
     st4(pdgc + j * D + d, san(pg.x + x.x * (bv.x * kv.x * eg.x), p.clip),
         san(pg.y + x.y * (bv.y * kv.y * eg.y), p.clip), san(pg.z + x.z * (bv.z * kv.z * eg.z), p.clip),
         san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
-  });
-  for_tile([&](int j, int d) {
-    const float4 x = lds4(t1 + j * TLD + d);
+    // dwv -> dw, dv (same pass: more independent loads in flight)
+    const float4 y = lds4(t1 + j * TLD + d);
     const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4<T>(wc + j * rs + d);
-    const float4 dw = make_float4(x.x * vv.x, x.y * vv.y, x.z * vv.z, x.w * vv.w);
-    const float4 dvv = make_float4(x.x * wv.x, x.y * wv.y, x.z * wv.z, x.w * wv.w);
+    const float4 dw = make_float4(y.x * vv.x, y.y * vv.y, y.z * vv.z, y.w * vv.w);
+    const float4 dvv = make_float4(y.x * wv.x, y.y * wv.y, y.z * wv.z, y.w * wv.w);
     st4<T>(dw_out + off + j * rs + d, san4(san4(dw, p.clip), kFinalClipTc));
     st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
   });
