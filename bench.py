@@ -71,8 +71,8 @@ def bytes_per_chunk(C, D):
 
 # DRAM bytes (read + write) per chunk from one ncu capture of config 1 at B=1
 # (384 chunks; traffic grows with the chunk count), profiles/tc_intra_kernels_config1_b1.md.
-NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 743_470, "bwd_intra1": 983_439, "bwd_intra2": 1_200_927,
-                         "bwd_intra3": 950_023}
+NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 743_297, "bwd_intra1": 970_652, "bwd_intra2": 1_199_843,
+                         "bwd_intra3": 952_852}
 
 
 class ClockSampler:
