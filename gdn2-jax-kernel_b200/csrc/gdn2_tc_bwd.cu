@@ -180,14 +180,10 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
     cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
   });
-  __syncthreads();
-  acc_to_smem<true>(tmem, 384, t0);    // t0[j][i] = dAqk(i, j)
-  __syncthreads();
   float* daqkT = ws.dAqkT + chunk * C * C;
-  for_tile([&](int j, int i) {
-    const float4 x = lds4(t0 + j * TLD + i);
-    st4(daqkT + j * C + i, j <= i ? san(x.x, p.clip) : 0.f, j <= i + 1 ? san(x.y, p.clip) : 0.f,
-        j <= i + 2 ? san(x.z, p.clip) : 0.f, j <= i + 3 ? san(x.w, p.clip) : 0.f);
+  for_acc<128>(tmem, 384, [&](int i, int c, const float* v) {   // dAqk^T, coalesced per column
+#pragma unroll
+    for (int t = 0; t < 16; ++t) daqkT[(c + t) * C + i] = c + t <= i ? san(v[t], p.clip) : 0.f;
   });
   {
     const int d = (threadIdx.x & 31) * 4;

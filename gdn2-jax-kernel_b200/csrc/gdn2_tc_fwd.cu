@@ -243,17 +243,15 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     }
   GDN2_TMARK(2);
     drain_n<kIss>(&ts.done, ph, ws.status);
-    acc_to_smem<true>(tmem, 0, t0);     // t0[j][i] = Aqk(i, j) / scale
-    acc_to_smem<true>(tmem, 128, S);    // S[j][i] = Akk(i, j)
-    __syncthreads();
-    for_tile([&](int j, int i) {
-      const float4 x = lds4(t0 + j * TLD + i), y = lds4(S + j * TLD + i);
-      sts4(aqkT + j * C + i,
-           make_float4(j <= i ? san(p.scale * x.x, p.clip) : 0.f, j <= i + 1 ? san(p.scale * x.y, p.clip) : 0.f,
-                       j <= i + 2 ? san(p.scale * x.z, p.clip) : 0.f, j <= i + 3 ? san(p.scale * x.w, p.clip) : 0.f));
-      sts4(S + j * TLD + i,
-           make_float4(j < i ? san(y.x, p.clip) : 0.f, j < i + 1 ? san(y.y, p.clip) : 0.f,
-                       j < i + 2 ? san(y.z, p.clip) : 0.f, j < i + 3 ? san(y.w, p.clip) : 0.f));
+    // straight from TMEM (lane = row i): for each column j a warp's stores are
+    // 32 consecutive i, coalesced in global memory and conflict-free in S
+    for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {   // Aqk / scale
+#pragma unroll
+      for (int t = 0; t < 16; ++t) aqkT[(c + t) * C + i] = c + t <= i ? san(p.scale * v[t], p.clip) : 0.f;
+    });
+    for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // S[j][i] = Akk(i, j)
+#pragma unroll
+      for (int t = 0; t < 16; ++t) S[(c + t) * TLD + i] = c + t < i ? san(v[t], p.clip) : 0.f;
     });
   } else {
     // exact elementwise form with the +-20 exponent clip (gdn2_fwd.py:124-139)
@@ -344,17 +342,17 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   }
   GDN2_TMARK(6);
   drain_n<kIss>(&ts.done, ph, ws.status);
-  float* u0 = sm;
-  float* u1 = sm + TILE_FLOATS;
-  acc_to_smem<true>(tmem, 0, u0);       // u0[d][i] = W(i, d)
-  acc_to_smem<false>(tmem, 128, u1);    // u1[i][d] = U(i, d)
-  __syncthreads();
   float* wt = ws.WT + chunk * C * D;
   float* uo = ws.U + chunk * C * D;
-  for_tile([&](int r, int cc) {
-    const float4 x = lds4(u0 + r * TLD + cc), y = lds4(u1 + r * TLD + cc);
-    sts4(wt + r * C + cc, make_float4(san(x.x, p.clip), san(x.y, p.clip), san(x.z, p.clip), san(x.w, p.clip)));
-    sts4(uo + r * D + cc, make_float4(san(y.x, p.clip), san(y.y, p.clip), san(y.z, p.clip), san(y.w, p.clip)));
+  for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {     // W^T, coalesced per column
+#pragma unroll
+    for (int t = 0; t < 16; ++t) wt[(c + t) * C + i] = san(v[t], p.clip);
+  });
+  for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // U, one row per lane
+#pragma unroll
+    for (int t = 0; t < 16; t += 4)
+      sts4(uo + i * D + c + t, make_float4(san(v[t], p.clip), san(v[t + 1], p.clip),
+                                           san(v[t + 2], p.clip), san(v[t + 3], p.clip)));
   });
   GDN2_TMARK(7);
   fence_before_sync();
