@@ -28,6 +28,7 @@ SIGNATURES = {
     "gdn2_bwd": (_i, [_i] + [_vp] * 6 + [_vp, _vp, _vp] + [_vp] * 6 + [_vp, _vp, _sz, _i]
                  + [_i] * 6 + [_f, _f, _vp]),
     "gdn2_fwd_noalloc": (_i, [_i] + [_vp] * 6 + [_vp, _vp, _vp] + [_i] * 6 + [_f, _f, _vp]),
+    "gdn2_decode": (_i, [_i] + [_vp] * 6 + [_vp, _vp, _vp] + [_i] * 4 + [_f, _f, _vp]),
     "gdn2_sp_segment": (_i, [_i, _vp, _sz, _vp, _vp, _vp] + [_i] * 6 + [_f, _f, _vp]),
     "gdn2_profile_enable": (_i, [_i]),
     "gdn2_selftest_gemm_tf32x3": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),

@@ -98,6 +98,16 @@ int gdn2_fwd_noalloc(int dtype, const void* q, const void* k, const void* v, con
                      int B, int T, int H, int D, int BT, int BC, float scale, float clip,
                      void* stream);
 
+/* Token-by-token decode of a short segment (B, T, H, D), carrying the state
+ * h0 (B,H,D,D, may be NULL = zero) to h_final: the recurrence of
+ * gdn2_pallas_forward (gdn2_fwd.py:338-362, state API gdn2_fwd.py:400-404)
+ * with chunks of one token, the CLIP sanitiser applied to o and to the state
+ * after every token.  One CTA per (batch, head), no workspace; the cost is
+ * linear in T with no chunk parallelism, so long prompts belong to gdn2_fwd. */
+int gdn2_decode(int dtype, const void* q, const void* k, const void* v, const void* w,
+                const void* b, const void* g, const float* h0, float* o, float* h_final, int B,
+                int T, int H, int D, float scale, float clip, void* stream);
+
 /* Per-launch device timing (test and benchmark support; no counterpart in the
  * reference).  When enabled, every kernel launch of gdn2_fwd / gdn2_bwd is
  * bracketed by CUDA events on its stream.  gdn2_profile_read() waits for the
