@@ -26,8 +26,9 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
     p = _fwd._Prepared(q, k, v, w, b, g, scale, h0)
     dev = p.dev
     do = torch.as_tensor(dout).to(device=dev, dtype=torch.float32, non_blocking=True).contiguous()
-    if tuple(do.shape) != (p.B, p.T, p.H, p.D):
-        raise _fwd.Gdn2ShapeError(f"dout must be {(p.B, p.T, p.H, p.D)}")
+    if tuple(do.shape) != (p.B, p.T_user, p.H, p.D):
+        raise _fwd.Gdn2ShapeError(f"dout must be {(p.B, p.T_user, p.H, p.D)}")
+    do = p.pad(do)
     if dh_final is None:
         dhf = torch.zeros((p.B, p.H, p.D, p.D), dtype=torch.float32, device=dev)
     else:
@@ -46,7 +47,7 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
         db.data_ptr(), dg.data_ptr(), dh0.data_ptr(), ws.data_ptr(), ws.numel(),
         int(residuals_valid), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip, p.stream)
     _lib.check(rc, "gdn2_bwd")
-    out = [dq, dk, dv, dw, db, dg]
+    out = [p.unpad(t) for t in (dq, dk, dv, dw, db, dg)]
     order = (0, 1, 2, 3, 4, 5)  # q k v w b g
     out = [t.to(p.in_dtypes[i]) for t, i in zip(out, order)]
     dh0 = dh0.to(p.h0_dtype)

@@ -36,6 +36,11 @@ CLIP = 1e4   # stage sanitiser bound
 # to float32 rounding unless a gate is positive and the +-20 exponent clip or
 # CLIP saturate (they act per chunk).
 EXACT_BT = True
+# T not a multiple of BT: the reference refuses it (gdn2_fwd.py:145-146), as
+# does this module by default.  MASKED_TAIL = True instead pads the sequence
+# with zero tokens (g = 0, k = q = v = w = b = 0), which leave the state and
+# every output and gradient of the real tokens unchanged, and slices back.
+MASKED_TAIL = False
 
 _GDN2_FWD_DIAG = os.environ.get("GDN2_FWD_DIAG", "0") == "1"
 _KERNEL_CHUNKS = (128, 64)
@@ -93,8 +98,11 @@ class _Prepared:
         B, T, H, D = shape
         if D not in _SUPPORTED_D:
             raise Gdn2ShapeError(f"head dim D={D} unsupported (64 or 128)")
-        self.B, self.T, self.H, self.D = B, T, H, D
         self.bt_user = int(BT)
+        self.T_user = T
+        if MASKED_TAIL and self.bt_user > 0 and T % self.bt_user:
+            T = -(-T // self.bt_user) * self.bt_user
+        self.B, self.T, self.H, self.D = B, T, H, D
         self.C = _kernel_chunk(T, self.bt_user, D)
         bc = int(BC)
         if bc <= 0 or self.bt_user % bc != 0:
@@ -113,6 +121,8 @@ class _Prepared:
         self.dtype = cdt
         self.code = _lib.F32 if cdt == torch.float32 else _lib.BF16
         self.t = tuple(t.to(device=dev, dtype=cdt, non_blocking=True).contiguous() for t in ts)
+        if T != self.T_user:
+            self.t = tuple(self.pad(t) for t in self.t)
         self.clip = float(CLIP)
         self.scale = float(scale)
         if h0 is None:
@@ -123,6 +133,16 @@ class _Prepared:
             self.h0_dtype = h0.dtype
             self.h0 = h0.to(device=dev, dtype=torch.float32, non_blocking=True).contiguous()
         self.stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def pad(self, t):
+        """(B, T_user, H, D) -> (B, T, H, D) with zero tokens at the end."""
+        if self.T == self.T_user:
+            return t
+        return torch.nn.functional.pad(t, (0, 0, 0, 0, 0, self.T - self.T_user)).contiguous()
+
+    def unpad(self, t):
+        """(B, T, H, D) -> (B, T_user, H, D)."""
+        return t if self.T == self.T_user else t[:, :self.T_user].contiguous()
 
     def ptrs(self):
         return [t.data_ptr() for t in self.t]
@@ -146,7 +166,7 @@ def _run_forward(p, save_residuals=False, ws=None):
                       int(save_residuals), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip,
                       p.stream)
     _lib.check(rc, "gdn2_fwd")
-    return o, h_final, ws
+    return p.unpad(o), h_final, ws
 
 
 def gdn2_pallas_forward(q, k, v, w, b, g, scale, h0=None, debug_tag=""):

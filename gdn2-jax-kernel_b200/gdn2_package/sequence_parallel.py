@@ -85,6 +85,8 @@ def sp_forward_local(q, k, v, w, b, g, scale, rank):
     p = _fwd._Prepared(q, k, v, w, b, g, scale, None)
     if not (p.C == 128 and p.D == 128):
         raise _fwd.Gdn2ShapeError("sequence parallelism needs BT = D = 128")
+    if p.T != p.T_user:
+        raise _fwd.Gdn2ShapeError("sequence parallelism needs segments divisible by BT")
     ws = p.workspace(True)
     o, c_seg, _ = _fwd._run_forward(p, save_residuals=True, ws=ws)
     P = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)

@@ -32,9 +32,10 @@ _alias_reference()
 @pytest.fixture(autouse=True)
 def _restore_constants():
     from gdn2_package import gdn2_fwd
-    saved = (gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP, gdn2_fwd.EXACT_BT)
+    saved = (gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP, gdn2_fwd.EXACT_BT, gdn2_fwd.MASKED_TAIL)
     yield
-    gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP, gdn2_fwd.EXACT_BT = saved
+    (gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP, gdn2_fwd.EXACT_BT,
+     gdn2_fwd.MASKED_TAIL) = saved
 
 
 def cuda_ok():

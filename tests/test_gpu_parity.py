@@ -99,6 +99,36 @@ def test_bt64_chunking_policy(exact):
         assert rel(a, b) < 1e-5, (name, rel(a, b))
 
 
+@pytest.mark.parametrize("D,BT,BC", [(128, 64, 16), (128, 128, 64), (64, 64, 16)])
+def test_masked_tail(D, BT, BC):
+    """T not a multiple of BT with MASKED_TAIL: the forward matches the float64
+    token recurrence, the gradients match the oracle's backward on explicitly
+    zero-padded inputs, restricted to the real tokens; the default refuses."""
+    from gdn2_package import gdn2_fwd
+    _set_consts(BT, BC, 1e4)
+    T = 200
+    inp = make_inputs(2, T, 2, D, seed=41, h0_std=0.1)
+    args = _dev(inp, torch.float32)
+    h0 = torch.as_tensor(inp["h0"]).cuda()
+    with pytest.raises(AssertionError):
+        gdn2_pallas_forward(*args, inp["scale"], h0)
+    gdn2_fwd.MASKED_TAIL = True
+    o, h = gdn2_pallas_forward(*args, inp["scale"], h0)
+    assert o.shape == (2, T, 2, D)
+    o_r, h_r = O.token_recurrence(*[inp[n] for n in NAMES], inp["scale"], inp["h0"])
+    assert rel(o, o_r) < 1e-5 and rel(h, h_r) < 1e-5, (rel(o, o_r), rel(h, h_r))
+    do = torch.as_tensor(inp["dout"]).cuda()
+    dhf = torch.as_tensor(inp["dh_final"]).cuda()
+    grads = gdn2_backward(*args, inp["scale"], h0, do, dhf)
+    Tp = -(-T // BT) * BT
+    padz = lambda a: np.concatenate([a, np.zeros((a.shape[0], Tp - T) + a.shape[2:], a.dtype)], 1)
+    g_r = O.backward(*[padz(inp[n]) for n in NAMES], inp["scale"], inp["h0"], padz(inp["dout"]),
+                     inp["dh_final"], BT, BC, 1e4)
+    for name, a, b in zip(GRADS, grads, g_r):
+        b = b[:, :T] if name != "dh0" else b
+        assert a.shape == b.shape and rel(a, b) < 1e-4, (name, rel(a, b))
+
+
 @pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64"])
 def test_against_reference_golden(name):
     """Outputs of the reference source itself (tests/golden/make_golden.py)."""
