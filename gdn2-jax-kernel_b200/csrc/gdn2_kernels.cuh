@@ -250,7 +250,7 @@ __device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
 enum Stage {
   kStageFwdIntra = 0, kStageFwdState, kStageBwdState, kStageBwdIntra1, kStageBwdIntra2,
   kStageBwdIntra3, kStageFwdAffine, kStageFwdScan, kStageFwdOut, kStageBwdPrep, kStageBwdScan,
-  kStageBwdDvn, kNumStages
+  kNumStages
 };
 
 // Called around every kernel launch of a multi-kernel launcher (no-op unless

@@ -89,7 +89,6 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   const float* doc = dout + off;
   const float* gc = ws.gc + chunk * C * D;
   const float* hpre = ws.hpre + chunk * D * D;
-  const float* dvn = ws.dv + chunk * C * D;
   const float* vnew = ws.vnew + chunk * C * D;
   const float* dhn = (c + 1 < p.nc) ? ws.dh + (chunk + 1) * D * D : dh_final + bh * D * D;
   float *pdq = ws.pdq + chunk * C * D, *pdk = ws.pdk + chunk * C * D,

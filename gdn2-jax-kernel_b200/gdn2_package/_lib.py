@@ -37,7 +37,7 @@ SIGNATURES = {
 }
 
 STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3",
-          "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan", "bwd_dvn")
+          "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan")
 
 
 def profile_enable(on=True):

@@ -113,7 +113,8 @@ int gdn2_decode(int dtype, const void* q, const void* k, const void* v, const vo
  * bracketed by CUDA events on its stream.  gdn2_profile_read() waits for the
  * recorded events and fills, per stage, the accumulated milliseconds and the
  * launch count (stages: 0 fwd_intra, 1 fwd_state, 2 bwd_state, 3 bwd_intra1,
- * 4 bwd_intra2, 5 bwd_intra3); it returns the number of stages. */
+ * 4 bwd_intra2, 5 bwd_intra3, 6 fwd_affine, 7 fwd_scan, 8 fwd_out, 9 bwd_prep,
+ * 10 bwd_scan); it returns the number of stages. */
 int gdn2_profile_enable(int on);
 int gdn2_profile_read(int n, double* total_ms, long* launches, int reset);
 
