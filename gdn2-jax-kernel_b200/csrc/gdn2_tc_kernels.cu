@@ -296,28 +296,42 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   {
     const Src srcs[3] = {trans(wt, C), trans(qgt, C, p.scale), trans(hp, D)};  // W, s qg, h^T
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // (W h)^T: (v, i)
+      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg h: (i, v)
     });
   }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
+  // vnew^T = U^T - (W h)^T, one TMEM lane per value column v: written to
+  // ws.vnew (coalesced per column i) and kept as four resident K-slices (rows
+  // v, K = i) in shared memory, the B operand of Aqk vnew.
   const float* u = ws.U + chunk * C * D;
   float* vn = ws.vnew + chunk * C * D;
-  for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
+  float* vt = sm;
+  for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
+    float* hi = vt + (c0 / KS) * 2 * SLICE_FLOATS;
+    float uu[16];   // all 16 loads issued before the stores to vnew (which may alias)
+#pragma unroll
+    for (int t = 0; t < 16; ++t) uu[t] = u[(c0 + t) * D + v];
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
-      const float4 uu = ld4f(u + i * D + c0 + j);
-      st4f(vn + i * D + c0 + j,
-           make_float4(uu.x - x[j], uu.y - x[j + 1], uu.z - x[j + 2], uu.w - x[j + 3]));
+      float y[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        y[t] = uu[j + t] - x[j + t];
+        vn[(c0 + j + t) * D + v] = y[t];
+      }
+      st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + j, KS, make_float4(y[0], y[1], y[2], y[3]));
     }
   });
-  __syncthreads();   // vnew (global) visible to the whole CTA
   const float* aqkt = ws.AqkT + chunk * C * C;
+  ring.base = sm + 4 * 2 * SLICE_FLOATS;
+  ring.nop = 1;
   {
-    const Src srcs[2] = {trans(aqkt, C), trans(vn, D)};   // (i,j) = Aqk, (v,j) = vnew(j,v)
+    const Src srcs[1] = {trans(aqkt, C)};   // (i,j) = Aqk
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1);
+      float* hi = vt + s * 2 * SLICE_FLOATS;
+      mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, 1);
     });
   }
   drain(&ts.done, ph, ws.status);
@@ -357,25 +371,38 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   {
     const Src srcs[3] = {direct(aqkt, C), direct(qgt, C, p.scale), trans(doc, rs)};  // (j,i) (d,i) (v,i)
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
-      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);
+      mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // dvp^T: (v, j)
+      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg^T do
     });
   }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
+  // dvp = san(Aqk^T do), one TMEM lane per value column v: written to ws.dvp
+  // (coalesced per column j) and kept as four resident K-slices (rows v,
+  // K = j) in shared memory, the B operand of -W^T dvp.
   float* dvp = ws.dvp + chunk * C * D;
-  for_acc<128>(tmem, 0, [&](int j, int c0, const float* x) {
+  float* dt = sm;
+  for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
+    float* hi = dt + (c0 / KS) * 2 * SLICE_FLOATS;
 #pragma unroll
-    for (int k = 0; k < 16; k += 4)
-      st4f(dvp + j * D + c0 + k, make_float4(san(x[k], p.clip), san(x[k + 1], p.clip),
-                                             san(x[k + 2], p.clip), san(x[k + 3], p.clip)));
+    for (int k = 0; k < 16; k += 4) {
+      float y[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        y[t] = san(x[k + t], p.clip);
+        dvp[(c0 + k + t) * D + v] = y[t];
+      }
+      st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + k, KS, make_float4(y[0], y[1], y[2], y[3]));
+    }
   });
-  __syncthreads();
   const float* wt = ws.WT + chunk * C * D;
+  ring.base = sm + 4 * 2 * SLICE_FLOATS;
+  ring.nop = 1;
   {
-    const Src srcs[2] = {direct(wt, C, -1.f), trans(dvp, D)};   // (d,j) = -W, (v,j) = dvp
+    const Src srcs[1] = {direct(wt, C, -1.f)};   // (d,j) = -W
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, 1);
+      float* hi = dt + s * 2 * SLICE_FLOATS;
+      mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, 1);
     });
   }
   drain(&ts.done, ph, ws.status);
