@@ -110,9 +110,12 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     float* dv = ws.dv + chunk * C * D;
     for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
       float hv[16], lv[16];
+      float4 av[4];   // loads first: the dv stores below may alias them for the compiler
+#pragma unroll
+      for (int k = 0; k < 4; ++k) av[k] = *reinterpret_cast<const float4*>(dvp + i * D + c0 + 4 * k);
 #pragma unroll
       for (int k = 0; k < 16; k += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(dvp + i * D + c0 + k);
+        const float4 a = av[k / 4];
         const float4 y = make_float4(san(a.x + x[k], p.clip), san(a.y + x[k + 1], p.clip),
                                      san(a.z + x[k + 2], p.clip), san(a.w + x[k + 3], p.clip));
         *reinterpret_cast<float4*>(dv + i * D + c0 + k) = y;
@@ -561,9 +564,12 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         if (pass == 0) {
 #pragma unroll
           for (int t = 0; t < 16; t += 4) xa[t / 4] = ld4<T>(qc + x * rs + c0 + t);
+          float4 pqv[4];   // loads before the aliasing gradient stores
+#pragma unroll
+          for (int t = 0; t < 4; ++t) pqv[t] = ldg4(pdq + x * D + c0 + 4 * t);
 #pragma unroll
           for (int t = 0; t < 16; t += 4) {
-            const float4 pq = ldg4(pdq + x * D + c0 + t);
+            const float4 pq = pqv[t / 4];
             const float* qv = &xa[t / 4].x;
             const float* pv = &pq.x;
             float o[4];
@@ -580,9 +586,12 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             xa[t / 4] = ld4<T>(kc + x * rs + c0 + t);
             xb[t / 4] = ld4<T>(bc + x * rs + c0 + t);
           }
+          float4 pbv[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) pbv[t] = ldg4(pdb + x * D + c0 + 4 * t);
 #pragma unroll
           for (int t = 0; t < 16; t += 4) {
-            const float4 pb = ldg4(pdb + x * D + c0 + t);
+            const float4 pb = pbv[t / 4];
             const float* kv = &xa[t / 4].x;
             const float* bv = &xb[t / 4].x;
             const float* pv = &pb.x;
@@ -609,9 +618,12 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             }
           }
           if (pass == 3) {
+            float4 pkv[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) pkv[t] = ldg4(pdk + x * D + c0 + 4 * t);
 #pragma unroll
             for (int t = 0; t < 16; t += 4) {
-              const float4 pk = ldg4(pdk + x * D + c0 + t);
+              const float4 pk = pkv[t / 4];
               const float* pv = &pk.x;
               float o[4];
 #pragma unroll
