@@ -1,0 +1,53 @@
+"""Host-side logic that needs no GPU: the chunk-length policy, argument
+checks that run before any CUDA call, and the bench's per-stage tables."""
+import importlib.util
+import os
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+
+def test_chunk_policy_exact_by_default():
+    from gdn2_package import gdn2_fwd
+    assert gdn2_fwd.EXACT_BT and not gdn2_fwd.MASKED_TAIL
+    k = gdn2_fwd._kernel_chunk
+    assert k(8192, 128, 128) == 128
+    assert k(8192, 64, 128) == 64          # exact BT: the CUDA-core kernels
+    assert k(8192, 256, 128) == 128        # BT = 256 runs as chunks of 128
+    assert k(256, 64, 64) == 64
+    with pytest.raises(AssertionError, match="divisible"):
+        k(100, 64, 128)
+    with pytest.raises(ValueError):
+        k(96, 32, 128)                     # no kernel runs chunks of 32
+
+
+def test_chunk_policy_tensor_core_opt_in():
+    from gdn2_package import gdn2_fwd
+    gdn2_fwd.EXACT_BT = False
+    k = gdn2_fwd._kernel_chunk
+    assert k(4096, 64, 128) == 128         # merged onto the tensor-core chunk
+    assert k(192, 64, 128) == 64           # T not a multiple of 128
+    assert k(256, 64, 64) == 64            # D = 64 has no tensor-core path
+
+
+def test_decode_rejects_unsupported_head_dim_before_cuda():
+    from gdn2_package import gdn2_decode
+    x = torch.zeros(1, 2, 1, 96)
+    with pytest.raises(ValueError, match="head dim"):
+        gdn2_decode(x, x, x, x, x, x, 0.1)
+    y = torch.zeros(1, 2, 1, 64)
+    with pytest.raises(ValueError, match="shape"):
+        gdn2_decode(x, y, y, y, y, y, 0.1)
+
+
+def test_bench_tables_cover_every_profiled_stage():
+    from gdn2_package import _lib
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    fl, by = bench.flops_per_chunk(128, 128), bench.bytes_per_chunk(128, 128)
+    assert set(_lib.STAGES) == set(fl) == set(by)
+    assert set(bench.NCU_TRAFFIC_PER_CHUNK) <= set(_lib.STAGES)
+    assert all(v > 0 for v in fl.values()) and all(v > 0 for v in by.values())
