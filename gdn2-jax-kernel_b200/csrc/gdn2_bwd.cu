@@ -1,6 +1,7 @@
 // GDN-2 fused backward: the reverse state pass (B1 with B2's dv_partial,
 // gdn2_bwd.py:45-80, 84-96) and three intra-chunk passes (B2's dAqk, B3, B4,
 // B5 and the final assembly of gdn2_pipeline.py:117-137).
+#include "gdn2_b4_exact.cuh"
 #include "gdn2_kernels.cuh"
 
 namespace gdn2 {
@@ -19,7 +20,7 @@ constexpr float kFinalClip = 1e4f;   // gdn2_pipeline.py:34
 template <int C, int D, int NV>
 __global__ void __launch_bounds__(kThreads, 2)
 k_bwd_state(Problem p, Workspace ws, const float* __restrict__ dout,
-            const float* __restrict__ dh_final, float* __restrict__ dh0) {
+            const float* __restrict__ dh_final, float* __restrict__ dh0, bool only_flagged) {
   using T1 = typename TileFor<C, NV>::type;
   using T3 = typename TileFor<D, NV>::type;
   constexpr int LDC = C + 4, LDD = D + 4;
@@ -31,6 +32,8 @@ k_bwd_state(Problem p, Workspace ws, const float* __restrict__ dout,
   const int v0 = blockIdx.x * NV, h = blockIdx.y, bb = blockIdx.z;
   const size_t bh = (size_t)bb * p.H + h;
   const long rs = p.row_stride();
+  // Exact recompute of the (b, h) the tensor-core scan's guard flagged.
+  if (only_flagged && ws.bnd[bh * p.nc * 4 + 3] == 0.f) return;
 
   for (int e = threadIdx.x; e < D * NV; e += kThreads) {
     const int d = e / NV, vv = e % NV;
@@ -408,7 +411,10 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
   float gpos = -1.f;
   for (int e = threadIdx.x; e < C * D; e += kThreads)
     gpos = fmaxf(gpos, to_f<T>(gcp[(e / D) * rs + e % D]));
-  const bool exact = block_max(gpos, red) > 0.f;
+  // positive gates, or sub-blocks that do not hold whole row groups (the
+  // clip guard below needs partials per BC block), take the exact path
+  const bool exact = block_max(gpos, red) > 0.f || p.bc % GS != 0;
+  bool run_exact = exact;
 
   if (!exact) {
     for (int e = threadIdx.x; e < NG * D; e += kThreads)
@@ -427,9 +433,38 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
     TD t;
     const int rg = t.r0 / GS;
     float dka[TD::TM_][TD::TN_];
+    // Clip guard.  The reference sanitises its B4 accumulators after every
+    // BC-row sub-block pair (_clip_acc, gdn2_bwd.py:26-28); summing all pairs
+    // at once gives the same value while the sum of the absolute per-block
+    // partials stays below CLIP.  grouped() runs the contraction one BC block
+    // at a time and leaves sum |block partial| per element in sab.
+    float sab[TD::TM_][TD::TN_];
+    const int gpb = p.bc / GS;   // row groups per sub-block
+    auto grouped = [&](int g0, int g1) {
+      t.zero();
+#pragma unroll
+      for (int i = 0; i < TD::TM_; ++i)
+#pragma unroll
+        for (int j = 0; j < TD::TN_; ++j) sab[i][j] = 0.f;
+      for (int a0 = g0; a0 < g1;) {
+        const int a1 = min(g1, (a0 / gpb + 1) * gpb);
+        TD tb;
+        tb.zero();
+        tb.mma_grouped(X1, LDC, X2, LDD, gref, D, a0, a1, rg);
+#pragma unroll
+        for (int i = 0; i < TD::TM_; ++i)
+#pragma unroll
+          for (int j = 0; j < TD::TN_; ++j) {
+            t.acc[i][j] += tb.acc[i][j];
+            sab[i][j] += fabsf(tb.acc[i][j]);
+          }
+        a0 = a1;
+      }
+    };
+    float gd_dq = 0.f, gd_dbk = 0.f, gd_dk2 = 0.f, gd_dk3 = 0.f;
+    float gg0 = 0.f, gg1 = 0.f, gg2 = 0.f, gg3 = 0.f;
     // dL_qk -> dq and dgc (i role)
-    t.zero();
-    t.mma_grouped(X1, LDC, X2, LDD, gref, D, 0, rg + 1, rg);
+    grouped(0, rg + 1);
 #pragma unroll
     for (int ii = 0; ii < TD::TM_; ++ii) {
       const int i = t.r0 + ii;
@@ -440,6 +475,8 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
         const float f = __expf(gc[i * D + d] - gc[t.r0 * D + d]);
         const float dl = t.acc[ii][jj] * f;
         o4[jj] = p.scale * to_f<T>(qc[i * rs + d]) * dl;
+        gd_dq = fmaxf(gd_dq, fabsf(p.scale) * sab[ii][jj] * f);
+        gg0 = fmaxf(gg0, fabsf(p.scale * to_f<T>(qc[i * rs + d])) * sab[ii][jj] * f);
         const float dq4 = san(p.scale * dl, p.clip);
         dq_out[off + i * rs + d] = from_f<T>(san(pdq[i * D + d] + dq4, kFinalClip));
       }
@@ -449,8 +486,7 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
     load_tile<float>(X1, LDC, dAkkT, C, C, C);
     __syncthreads();
     // dL_kk = dbk -> db, dk (b branch), dgc (i role)
-    t.zero();
-    t.mma_grouped(X1, LDC, X2, LDD, gref, D, 0, rg + 1, rg);
+    grouped(0, rg + 1);
 #pragma unroll
     for (int ii = 0; ii < TD::TM_; ++ii) {
       const int i = t.r0 + ii;
@@ -460,6 +496,8 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
         const float f = __expf(gc[i * D + d] - gc[t.r0 * D + d]);
         const float dbk = t.acc[ii][jj] * f;
         const float kk = to_f<T>(kc[i * rs + d]), bv = to_f<T>(bc[i * rs + d]);
+        gd_dbk = fmaxf(gd_dbk, sab[ii][jj] * f);
+        gg1 = fmaxf(gg1, fabsf(bv * kk) * sab[ii][jj] * f);
         dka[ii][jj] = dbk * bv;
         sdg[i * D + d] += bv * kk * dbk;
         db_out[off + i * rs + d] =
@@ -479,17 +517,19 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
           p.scale * qv.z * __expf(gi[2] - gr[2]), p.scale * qv.w * __expf(gi[3] - gr[3]));
     }
     __syncthreads();
-    t.zero();
-    t.mma_grouped(X1, LDC, X2, LDD, gref, D, rg, NG, rg);
+    grouped(rg, NG);
 #pragma unroll
     for (int ii = 0; ii < TD::TM_; ++ii) {
       const int j = t.r0 + ii;
 #pragma unroll
       for (int jj = 0; jj < TD::TN_; ++jj) {
         const int d = t.c0 + jj;
-        const float dr = t.acc[ii][jj] * __expf(gc[t.r0 * D + d] - gc[j * D + d]);
+        const float fr = __expf(gc[t.r0 * D + d] - gc[j * D + d]);
+        const float dr = t.acc[ii][jj] * fr;
         dka[ii][jj] += dr;
         sdg[j * D + d] -= to_f<T>(kc[j * rs + d]) * dr;
+        gd_dk2 = fmaxf(gd_dk2, sab[ii][jj] * fr);
+        gg2 = fmaxf(gg2, fabsf(to_f<T>(kc[j * rs + d])) * sab[ii][jj] * fr);
       }
     }
     __syncthreads();
@@ -505,57 +545,32 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
           bv.z * kv.z * __expf(gi[2] - gr[2]), bv.w * kv.w * __expf(gi[3] - gr[3]));
     }
     __syncthreads();
-    t.zero();
-    t.mma_grouped(X1, LDC, X2, LDD, gref, D, rg, NG, rg);
+    grouped(rg, NG);
 #pragma unroll
     for (int ii = 0; ii < TD::TM_; ++ii) {
       const int j = t.r0 + ii;
 #pragma unroll
       for (int jj = 0; jj < TD::TN_; ++jj) {
         const int d = t.c0 + jj;
-        const float dr = t.acc[ii][jj] * __expf(gc[t.r0 * D + d] - gc[j * D + d]);
+        const float fr = __expf(gc[t.r0 * D + d] - gc[j * D + d]);
+        const float dr = t.acc[ii][jj] * fr;
+        gd_dk3 = fmaxf(gd_dk3, sab[ii][jj] * fr);
+        gg3 = fmaxf(gg3, fabsf(to_f<T>(kc[j * rs + d])) * sab[ii][jj] * fr);
         const float dk4 = san(dka[ii][jj] + dr, p.clip);
         dk_out[off + j * rs + d] = from_f<T>(san(pdk[j * D + d] + dk4, kFinalClip));
         const float x = sdg[j * D + d] - to_f<T>(kc[j * rs + d]) * dr;
         sdg[j * D + d] = pdgc[j * D + d] + san(x, p.clip);
       }
     }
-  } else {
-    // exact elementwise form (gdn2_bwd.py:298-328) for chunks with g > 0
-    for (int e = threadIdx.x; e < C * D; e += kThreads) {
-      const int x = e / D, d = e % D;
-      const float kx = to_f<T>(kc[x * rs + d]), bx = to_f<T>(bc[x * rs + d]);
-      const float lq = p.scale * to_f<T>(qc[x * rs + d]), lk = bx * kx;
-      float dlq = 0.f, dlk = 0.f, drq = 0.f, drk = 0.f, dgi = 0.f, dgj = 0.f;
-      for (int y = 0; y < C; ++y) {
-        if (y <= x) {   // x as row i, y as column j
-          const float dd = gc[x * D + d] - gc[y * D + d];
-          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
-          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
-          const float mq = dAqkT[y * C + x], mk = (y < x) ? dAkkT[y * C + x] : 0.f;
-          const float ry = to_f<T>(kc[y * rs + d]) * ed;
-          dlq = fmaf(mq, ry, dlq);
-          dlk = fmaf(mk, ry, dlk);
-          dgi += (mq * lq + mk * lk) * ry * cm;
-        }
-        if (y >= x) {   // x as column j, y as row i
-          const float dd = gc[y * D + d] - gc[x * D + d];
-          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
-          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
-          const float mq = dAqkT[x * C + y], mk = (y > x) ? dAkkT[x * C + y] : 0.f;
-          const float lqy = p.scale * to_f<T>(qc[y * rs + d]) * ed;
-          const float lky = to_f<T>(bc[y * rs + d]) * to_f<T>(kc[y * rs + d]) * ed;
-          drq = fmaf(mq, lqy, drq);
-          drk = fmaf(mk, lky, drk);
-          dgj += (mq * lqy + mk * lky) * kx * cm;
-        }
-      }
-      dq_out[off + x * rs + d] = from_f<T>(san(pdq[e] + san(p.scale * dlq, p.clip), kFinalClip));
-      db_out[off + x * rs + d] = from_f<T>(san(pdb[e] + san(dlk * kx, p.clip), kFinalClip));
-      dk_out[off + x * rs + d] =
-          from_f<T>(san(pdk[e] + san(drq + drk + dlk * bx, p.clip), kFinalClip));
-      sdg[e] = pdgc[e] + san(dgi - dgj, p.clip);
-    }
+    const float lim = p.clip * (1.f - 1e-5f);   // NaN fails every test below
+    run_exact = __syncthreads_or(!(gd_dq < lim && gd_dbk < lim && gd_dk2 + gd_dk3 < lim &&
+                                   gg0 + gg1 + gg2 + gg3 < lim));
+    if (run_exact && threadIdx.x == 0) atomicOr(ws.status + 4, 1);
+  }
+  if (run_exact) {
+    // the reference's pair order (overwrites the fast path's outputs)
+    b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, D, dAqkT, dAkkT, pdq, pdk, pdb, pdgc,
+                      dq_out, dk_out, db_out, off, sdg, p.scale, p.clip);
   }
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);
@@ -568,13 +583,14 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
 // ---------------------------------------------------------------------------
 template <int C, int D>
 cudaError_t launch_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
-                             const float* dh_final, float* dh0, cudaStream_t s) {
+                             const float* dh_final, float* dh0, cudaStream_t s,
+                             bool only_flagged) {
   constexpr int NV = 32;
   const size_t smem = StateSmem<C, D, NV>::bytes();
   auto kern = k_bwd_state<C, D, NV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(D / NV, p.H, p.B), kThreads, smem, s>>>(p, ws, dout, dh_final, dh0);
+  kern<<<dim3(D / NV, p.H, p.B), kThreads, smem, s>>>(p, ws, dout, dh_final, dh0, only_flagged);
   return cudaGetLastError();
 }
 
@@ -624,7 +640,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
 
 #define GDN2_INST_BSTATE(C, D)                                                               \
   template cudaError_t launch_bwd_state<C, D>(const Problem&, const Workspace&, const float*, \
-                                              const float*, float*, cudaStream_t);
+                                              const float*, float*, cudaStream_t, bool);
 #define GDN2_INST_BINTRA(T, C, D)                                                            \
   template cudaError_t launch_bwd_intra<T, C, D>(                                            \
       const T*, const T*, const T*, const T*, const T*, const T*, const float*, const float*, \

@@ -72,6 +72,10 @@ int validate(int dtype, int B, int T, int H, int D, int BT, int BC, float scale,
     return fail(GDN2_ERR_INVALID, "%sT=%ld must be divisible by BT=%ld", "", T, BT);
   if (BC <= 0 || BT % BC != 0)
     return fail(GDN2_ERR_INVALID, "%ssub-block BC=%ld must divide BT=%ld", "", BC, BT);
+  // the reference's block solve runs MB = 16 micro-blocks inside each BC
+  // sub-block (gdn2_fwd.py:32, 194)
+  if (BC % 16 != 0)
+    return fail(GDN2_ERR_INVALID, "%ssub-block BC=%ld must be a multiple of MB=16", "", BC);
   if (!(clip > 0.f)) return fail(GDN2_ERR_INVALID, "%sclip must be positive");
   if (scale != scale) return fail(GDN2_ERR_INVALID, "%sscale is NaN");
   return GDN2_OK;
@@ -155,9 +159,16 @@ int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
 // (affine scan, gdn2_tc_kernels.cu); other shapes use the CUDA-core kernels.
 bool use_tc(int BT, int D) { return BT == 128 && D == 128; }
 
-Problem make_problem(int B, int T, int H, int D, int BT, float scale, float clip) {
+// Every entry point clears the status header of its workspace first, so the
+// word gdn2_workspace_status() reads belongs to the latest call.
+int clear_status(const Workspace& ws, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(ws.status, 0, 256, s);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "status reset");
+}
+
+Problem make_problem(int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
   Problem p;
-  p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT;
+  p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT; p.bc = BC;
   p.scale = scale; p.clip = clip;
   return p;
 }
@@ -173,7 +184,29 @@ int report_error(int code, const char* msg) {
 }
 }  // namespace gdn2
 
+// Byte offset of the status header inside a caller workspace (the first
+// 256-byte boundary at or after its start, as Workspace::carve places it).
+size_t gdn2_status_offset(const void* workspace) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(workspace);
+  return (size_t)(((a + 255) & ~(uintptr_t)255) - a);
+}
+
 extern "C" {
+
+int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < 512)
+    return fail(GDN2_ERR_INVALID, "%sgdn2_workspace_status: null or undersized workspace");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int* st = reinterpret_cast<const int*>(static_cast<const char*>(workspace) +
+                                               gdn2_status_offset(workspace));
+  int host[5] = {0, 0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyAsync(host, st, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_workspace_status");
+  return (host[0] ? GDN2_STATUS_WAIT_TIMEOUT : 0) | (host[1] ? GDN2_STATUS_FWD_STATE_CLIPPED : 0) |
+         (host[2] ? GDN2_STATUS_BWD_STATE_CLIPPED : 0) | (host[3] ? GDN2_STATUS_EXACT_RECOMPUTE : 0) |
+         (host[4] ? GDN2_STATUS_B4_EXACT : 0);
+}
 
 int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }
 
@@ -223,9 +256,10 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, false);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = clear_status(ws, s))) return rc;
   rc = dtype == GDN2_F32
            ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
            : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
@@ -251,9 +285,10 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, true);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = clear_status(ws, s))) return rc;
   if (!residuals_valid) {
     // The reference's custom_vjp keeps only the inputs and recomputes the
     // forward in the backward (gdn2_pipeline.py:64-83); o is not needed.
@@ -298,8 +333,9 @@ int gdn2_sp_segment(int op, void* workspace, size_t workspace_bytes, const float
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const Problem p = make_problem(B, T, H, D, BT, scale, clip);
+  const Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, bwd);
+  if ((rc = clear_status(ws, static_cast<cudaStream_t>(stream)))) return rc;
   cudaError_t e = launch_tc_sp(op, p, ws, in, o, out, static_cast<cudaStream_t>(stream), hook());
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "sp_segment");
 }

@@ -137,7 +137,7 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
   __syncthreads();
 
   // ---- Kernel B: A = (I + Akk)^-1, computed in place on the transpose.
-  wy_inverse_T<C>(X, LDC, Y, p.clip);
+  wy_inverse_T<C>(X, LDC, Y, p.bc, p.clip);
   {
     float* at = ws.AT + chunk * C * C;
     for (int e = threadIdx.x * 4; e < C * C; e += kThreads * 4) {

@@ -36,54 +36,87 @@ template <int C, int D, int NV> struct StateSmem {
   static size_t bytes() { return (size_t)(BIG + D * NV + 2 * C * NV) * sizeof(float); }
 };
 
-// In-place (I + T)^-1 for a strictly lower-triangular C x C matrix held
-// transposed in shared memory: on entry S[j*ld + i] = T(i, j), on exit
-// S[j*ld + i] = A(i, j).  16 x 16 diagonal blocks are inverted by row-wise
-// forward substitution (gdn2_fwd.py:174-189), then blocks are composed by
-// doubling, A10 = -A11 (T10 A00), the recurrence of gdn2_fwd.py:202-211 and
-// 235-238, sanitising each product as the reference does.
-// `tmp` needs C*C/4 floats.
+// Block forward substitution of (I + T)^-1 in the reference's order
+// (_block_solve, gdn2_fwd.py:192-222; Kernel B's sub-block step,
+// gdn2_fwd.py:225-243, generalised from two sub-blocks to nb): within every
+// group of nb diagonal blocks of size blk whose diagonal blocks already hold
+// their inverses,
+//     for m = 1 .. nb-1, n = m-1 .. 0:
+//         acc = 0;  for k = n .. m-1:  acc = san(acc + T_mk A_kn)
+//         A_mn = san(-A_mm acc)
+// S is transposed (S[j*ld + i] = M(i, j)), holding T below the processed
+// rows and A elsewhere.  `tmp` needs (nb-1) * blk^2 * (C / (blk*nb)) floats.
+__device__ __forceinline__ void wy_compose_seq(float* S, int ld, int C, int blk, int nb, float* tmp,
+                                               float clip) {
+  const int per = blk * blk, groups = C / (blk * nb);
+  for (int m = 1; m < nb; ++m) {
+    const int total = groups * m * per;
+    for (int e = threadIdx.x; e < total; e += kThreads) {   // acc_n of every block (m, n)
+      const int gi = e / (m * per), rem = e % (m * per), n = rem / per, r2 = rem % per;
+      const int i = r2 % blk, j = r2 / blk, o = gi * blk * nb;
+      const int row = o + m * blk + i, col = o + n * blk + j;
+      float acc = 0.f;
+      for (int k = n; k < m; ++k) {
+        const int x0 = o + k * blk;
+        float sum = 0.f;
+        for (int t = 0; t < blk; ++t) sum = fmaf(S[(x0 + t) * ld + row], S[col * ld + x0 + t], sum);
+        acc = san(acc + sum, clip);
+      }
+      tmp[(gi * (nb - 1) + n) * per + j * blk + i] = acc;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < total; e += kThreads) {   // A_mn = san(-A_mm acc_n)
+      const int gi = e / (m * per), rem = e % (m * per), n = rem / per, r2 = rem % per;
+      const int i = r2 % blk, j = r2 / blk, o = gi * blk * nb;
+      const int row = o + m * blk + i, col = o + n * blk + j;
+      const float* an = tmp + (gi * (nb - 1) + n) * per + j * blk;
+      const int x0 = o + m * blk;
+      float sum = 0.f;
+      for (int t = 0; t < blk; ++t) sum = fmaf(S[(x0 + t) * ld + row], an[t], sum);
+      S[col * ld + row] = san(-sum, clip);
+    }
+    __syncthreads();
+  }
+}
+
+// Row-by-row forward substitution of every 16 x 16 diagonal block
+// (_micro_forward_substitution, gdn2_fwd.py:174-189), in place on the
+// transposed S; one warp per block, one lane per column of A.
 template <int C>
-__device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, float clip) {
+__device__ __forceinline__ void wy_micro_solves(float* S, int ld, float clip) {
   constexpr int MBK = 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp < C / MBK && lane < MBK) {
-    const int o = warp * MBK, jj = lane;
-    float x[MBK];
+  for (int blkid = warp; blkid < C / MBK; blkid += kThreads / 32) {
+    if (lane < MBK) {
+      const int o = blkid * MBK, jj = lane;
+      float x[MBK];
 #pragma unroll
-    for (int r = 0; r < MBK; ++r) {
-      float s = 0.f;
+      for (int r = 0; r < MBK; ++r) {
+        float s = 0.f;
 #pragma unroll
-      for (int t = 0; t < r; ++t) s = fmaf(S[(o + t) * ld + o + r], x[t], s);
-      x[r] = (r < jj) ? 0.f : (r == jj ? san(1.f - s, clip) : san(-s, clip));
+        for (int t = 0; t < r; ++t) s = fmaf(S[(o + t) * ld + o + r], x[t], s);
+        x[r] = (r < jj) ? 0.f : (r == jj ? san(1.f - s, clip) : san(-s, clip));
+      }
+      __syncwarp(0x0000ffffu);
+#pragma unroll
+      for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
     }
-    __syncwarp(0x0000ffffu);
-#pragma unroll
-    for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
   }
   __syncthreads();
-#pragma unroll 1
-  for (int s = 2 * MBK; s <= C; s *= 2) {
-    const int half = s / 2, per = half * half, total = (C / s) * per;
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
-      const int o = beta * s;
-      float acc = 0.f;
-      for (int kk = j; kk < half; ++kk)
-        acc = fmaf(S[(o + kk) * ld + o + half + i], S[(o + j) * ld + o + kk], acc);
-      tmp[beta * per + j * half + i] = san(acc, clip);
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      const int beta = e / per, rem = e % per, i = rem % half, j = rem / half;
-      const int o = beta * s;
-      float acc = 0.f;
-      for (int kk = 0; kk <= i; ++kk)
-        acc = fmaf(S[(o + half + kk) * ld + o + half + i], tmp[beta * per + j * half + kk], acc);
-      S[(o + j) * ld + o + half + i] = san(-acc, clip);
-    }
-    __syncthreads();
-  }
+}
+
+// In-place A = (I + T)^-1 for a strictly lower-triangular C x C matrix held
+// transposed in shared memory (on entry S[j*ld + i] = T(i, j), on exit
+// S[j*ld + i] = A(i, j)), in the reference's order: 16 x 16 micro solves,
+// the block substitution of the 16-row blocks inside every BC sub-block
+// (_block_solve), then of the BC sub-blocks (Kernel B).  Every product is
+// sanitised where the reference sanitises it, so the result matches it also
+// when CLIP acts.  BC is a multiple of 16 dividing C.  `tmp` needs C*C/4 floats.
+template <int C>
+__device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, int bc, float clip) {
+  wy_micro_solves<C>(S, ld, clip);
+  if (bc > 16) wy_compose_seq(S, ld, C, 16, bc / 16, tmp, clip);
+  if (C > bc) wy_compose_seq(S, ld, C, bc, C / bc, tmp, clip);
 }
 
 // Column-wise inclusive prefix sum of a C x D tile held row-major in shared
@@ -166,29 +199,21 @@ __device__ __forceinline__ void wy_level_tiled(float* S, int ld, float* tmp, flo
   __syncthreads();
 }
 
-// wy_inverse_T for C = 128 with the last doubling level (two 64 x 64 x 64
-// products) on register tiles.  `tmp` needs 4096 floats, `scr` 2 * 64 * 68.
-__device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr,
+// wy_inverse_T for C = 128.  For BC = 64 (two sub-blocks) the sub-block
+// step is the two 64 x 64 x 64 products tmp = san(T10 A00),
+// A10 = san(-A11 tmp) on register tiles; for BC = 32 the 16-row step inside a
+// sub-block is one register-tiled level.  Other BC take the generic
+// substitution.  `tmp` needs 4096 floats, `scr` 2 * 64 * 68.
+__device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr, int bc,
                                                 float clip) {
-  constexpr int MBK = 16, C = 128, H = 64, LY = 68;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane < MBK) {
-    const int o = warp * MBK, jj = lane;
-    float x[MBK];
-#pragma unroll
-    for (int r = 0; r < MBK; ++r) {
-      float s = 0.f;
-#pragma unroll
-      for (int t = 0; t < r; ++t) s = fmaf(S[(o + t) * ld + o + r], x[t], s);
-      x[r] = (r < jj) ? 0.f : (r == jj ? san(1.f - s, clip) : san(-s, clip));
-    }
-    __syncwarp(0x0000ffffu);
-#pragma unroll
-    for (int r = 0; r < MBK; ++r) S[(o + jj) * ld + o + r] = x[r];
+  constexpr int C = 128, H = 64, LY = 68;
+  wy_micro_solves<C>(S, ld, clip);
+  if (bc == 32) wy_level_tiled<16, 2, 2>(S, ld, tmp, clip);            // two 16-row blocks
+  else if (bc > 16) wy_compose_seq(S, ld, C, 16, bc / 16, tmp, clip);   // inside each sub-block
+  if (bc != 64) {
+    if (C > bc) wy_compose_seq(S, ld, C, bc, C / bc, tmp, clip);
+    return;
   }
-  __syncthreads();
-  wy_level_tiled<16, 2, 2>(S, ld, tmp, clip);   // blocks of 32
-  wy_level_tiled<32, 2, 4>(S, ld, tmp, clip);   // blocks of 64
   // last level: T10 = M(64.., 0..63), A00 = A(0..63, 0..63), A11 = A(64.., 64..)
   float* y = scr;             // y[k][j] = A00(k, j)   (row-major copy)
   float* t = scr + H * LY;    // t[k][j] = tmp(k, j)
@@ -250,7 +275,7 @@ __device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
 enum Stage {
   kStageFwdIntra = 0, kStageFwdState, kStageBwdState, kStageBwdIntra1, kStageBwdIntra2,
   kStageBwdIntra3, kStageFwdAffine, kStageFwdScan, kStageFwdOut, kStageBwdPrep, kStageBwdScan,
-  kNumStages
+  kStageBwdExact, kNumStages
 };
 
 // Called around every kernel launch of a multi-kernel launcher (no-op unless
@@ -270,7 +295,8 @@ cudaError_t launch_fwd_state(const Problem& p, const Workspace& ws, const float*
                              float* hfinal, int save, cudaStream_t s);
 template <int C, int D>
 cudaError_t launch_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
-                             const float* dh_final, float* dh0, cudaStream_t s);
+                             const float* dh_final, float* dh0, cudaStream_t s,
+                             bool only_flagged = false);
 template <typename T, int C, int D>
 cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,

@@ -70,8 +70,16 @@ extern "C" int gdn2_fwd_noalloc(int dtype, const void* q, const void* k, const v
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc) return rc;
-  // The forward writes every workspace tile before reading it, so the
-  // previous call's contents need no clearing.
+  // The forward writes every workspace tile before reading it, and gdn2_fwd
+  // clears the status header first, so the previous call's contents need no
+  // other clearing.
   return gdn2_fwd(dtype, q, k, v, w, b, g, h0, o, h_final, scratch, kScratchBytes,
                   /*save_residuals=*/0, B, T, H, D, BT, BC, scale, clip, stream);
+}
+
+extern "C" int gdn2_noalloc_status(void* stream) {
+  void* scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  return gdn2_workspace_status(scratch, kScratchBytes, stream);
 }

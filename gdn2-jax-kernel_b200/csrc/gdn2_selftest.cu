@@ -91,7 +91,32 @@ k_selftest_gemm(const float* __restrict__ A, const float* __restrict__ B, float*
   if (warp == 0) tc::tmem_free(tmem, ncols);
 }
 
+// One warp waits on an mbarrier that nothing ever arrives on, with a short
+// poll limit: the wait gives up, records kErrWaitTimeout in *status and the
+// kernel returns.  No TMEM, no MMA and no copy is in flight.
+__global__ void k_selftest_wait_timeout(int* status, long long polls) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  tc::mbar_wait(&bar, 0, status, polls);
+}
+
 }  // namespace gdn2
+
+size_t gdn2_status_offset(const void* workspace);
+
+extern "C" int gdn2_selftest_wait_timeout(void* workspace, size_t workspace_bytes, int polls,
+                                          void* stream) {
+  if (!workspace || workspace_bytes < 512 || polls <= 0) return GDN2_ERR_INVALID;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = reinterpret_cast<int*>(static_cast<char*>(workspace) + gdn2_status_offset(workspace));
+  if (cudaMemsetAsync(status, 0, 256, s) != cudaSuccess) return GDN2_ERR_CUDA;
+  gdn2::k_selftest_wait_timeout<<<1, 32, 0, s>>>(status, polls);
+  return cudaGetLastError() == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
+}
 
 extern "C" int gdn2_selftest_gemm_tf32x3(const float* A, const float* B, float* D, int batch,
                                          int K, int N, int trans_a, int trans_b, int* status,

@@ -13,7 +13,8 @@
 // staged instead.
 //
 // Every wait on an mbarrier is bounded; on expiry the kernel records an error
-// code in a caller-provided device status word and proceeds.
+// code in a caller-provided device status word and proceeds (its results are
+// then invalid; the C ABI reports the word through gdn2_workspace_status).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -154,9 +155,10 @@ constexpr int kErrWaitTimeout = 1;
 constexpr long long kWaitLimit = 1ll << 22;
 
 // Wait for the phase with parity `parity` of `bar` to complete; bounded.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          long long limit = kWaitLimit) {
   const uint32_t a = smem_u32(bar);
-  for (long long it = 0; it < kWaitLimit; ++it) {
+  for (long long it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"

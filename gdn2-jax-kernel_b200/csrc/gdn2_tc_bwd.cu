@@ -2,6 +2,7 @@
 // chunk = head dim = 128 path.  Same contracts as k_bwd_intra1 / k_bwd_intra2
 // in gdn2_bwd.cu (B2's dAqk and B3, gdn2_bwd.py:84-96, 126-210); every
 // product runs as a 128 x 128 x 128 3xTF32 MMA into TMEM.
+#include "gdn2_b4_exact.cuh"
 #include "gdn2_kernels.cuh"
 #include "gdn2_tc_stage.cuh"
 
@@ -97,9 +98,13 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   Ring ring = ring_of(sm, &ts, 2);
   int g = 0;
   uint32_t ph = 0;
-  // dv = san(dvp + kg dh_next)  (TMEM 0, contraction over d)
+  // dv = san(dvp + kg dh_next)  (TMEM 0, contraction over d).  B1 carries
+  // the sanitised dh_final into the last chunk (gdn2_bwd.py:53), while B3's
+  // dh_next is the raw dh_final (gdn2_pipeline.py:52-56): only this product
+  // sees it clipped.
   {
-    const Src srcs[2] = {direct(ws.kg + chunk * C * D, D), trans(dhn, D)};   // (i,d), (v,d)
+    const float dclip = (c + 1 < p.nc) ? 0.f : p.clip;
+    const Src srcs[2] = {direct(ws.kg + chunk * C * D, D), trans(dhn, D, 1.f, dclip)};   // (i,d), (v,d)
     kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
     });
@@ -479,8 +484,12 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     spread = fmaxf(spread, fabsf(gc[(32 * J) * GLD + d] - gc[(32 * J + 31) * GLD + d]));
     if (J < 2) spread64 = fmaxf(spread64, fabsf(gc[(64 * J) * GLD + d] - gc[(64 * J + 63) * GLD + d]));
   }
-  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
-  const int JW = block_max(spread64, red) <= 80.f ? 64 : 32;
+  // The fast path's column blocks must nest inside the reference's BC-row
+  // sub-blocks for its clip guard (below) to hold, so BC < 32 takes the exact
+  // pair-ordered path.
+  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread || p.bc < 32;
+  const int JW = (block_max(spread64, red) <= 80.f && p.bc % 64 == 0) ? 64 : 32;
+  bool run_exact = exact;
 
   if (!exact) {
     Ring ring = ring_of(sm, &ts, 2);
@@ -492,6 +501,14 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     float dkr[64], dgr[64];
 #pragma unroll
     for (int t = 0; t < 64; ++t) dkr[t] = dgr[t] = 0.f;
+    // Clip guard.  The reference sanitises its B4 accumulators after every
+    // BC-row sub-block pair (_clip_acc); summing all pairs at once gives the
+    // same value while no prefix of that sequence reaches CLIP, which holds
+    // when the sum of the absolute block partials stays below CLIP (the JW
+    // blocks nest in the BC blocks, so every reference prefix is a sum of
+    // them).  Per thread: the largest such sum of each accumulator.
+    float gq_dq = 0.f, gq_dbk = 0.f, gq_dk2 = 0.f, gq_dk3 = 0.f;
+    float gg0 = 0.f, gg1 = 0.f, gg2 = 0.f, gg3 = 0.f;   // dgc terms of each pass
 #pragma unroll 1
     for (int pass = 0; pass < 4; ++pass) {
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
@@ -539,12 +556,14 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         float val[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) val[t] = 0.f;
-        float gx[16];
+        float gx[16], sab[16];
 #pragma unroll
         for (int t = 0; t < 16; t += 4) {
           const float4 v4 = ldg4(gc + x * GLD + c0 + t);
           gx[t] = v4.x; gx[t + 1] = v4.y; gx[t + 2] = v4.z; gx[t + 3] = v4.w;
         }
+#pragma unroll
+        for (int t = 0; t < 16; ++t) sab[t] = 0.f;
 #pragma unroll
         for (int J = 0; J < 4; ++J) {
           if (J >= C / JW) break;
@@ -556,7 +575,9 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
               const float gr = gc[r * GLD + c0 + t];
-              val[t] += a[t] * __expf(left ? gx[t] - gr : gr - gx[t]);
+              const float part = a[t] * __expf(left ? gx[t] - gr : gr - gx[t]);
+              val[t] += part;
+              sab[t] += fabsf(part);
             }
           }
         }
@@ -577,6 +598,8 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             for (int u = 0; u < 4; ++u) {
               o[u] = san(pv[u] + san(p.scale * val[t + u], p.clip), kFinalClipTc);
               dgr[qd * 16 + t + u] += p.scale * qv[u] * val[t + u];
+              gq_dq = fmaxf(gq_dq, fabsf(p.scale) * sab[t + u]);
+              gg0 = fmaxf(gg0, fabsf(p.scale * qv[u]) * sab[t + u]);
             }
             st4<T>(dq_out + off + x * rs + c0 + t, make_float4(o[0], o[1], o[2], o[3]));
           }
@@ -602,6 +625,8 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
               o[u] = san(pv[u] + san(dbk * kv[u], p.clip), kFinalClipTc);
               dkr[qd * 16 + t + u] = dbk * bv[u];
               dgr[qd * 16 + t + u] += bv[u] * kv[u] * dbk;
+              gq_dbk = fmaxf(gq_dbk, sab[t + u]);
+              gg1 = fmaxf(gg1, fabsf(bv[u] * kv[u]) * sab[t + u]);
             }
             st4<T>(db_out + off + x * rs + c0 + t, make_float4(o[0], o[1], o[2], o[3]));
           }
@@ -615,6 +640,13 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             for (int u = 0; u < 4; ++u) {
               dkr[qd * 16 + t + u] += val[t + u];
               dgr[qd * 16 + t + u] -= kv[u] * val[t + u];
+              if (pass == 2) {
+                gq_dk2 = fmaxf(gq_dk2, sab[t + u]);
+                gg2 = fmaxf(gg2, fabsf(kv[u]) * sab[t + u]);
+              } else {
+                gq_dk3 = fmaxf(gq_dk3, sab[t + u]);
+                gg3 = fmaxf(gg3, fabsf(kv[u]) * sab[t + u]);
+              }
             }
           }
           if (pass == 3) {
@@ -635,8 +667,12 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         }
       }
     }
+    const float lim = p.clip * (1.f - 1e-5f);   // NaN fails every test below
+    const bool bad = !(gq_dq < lim && gq_dbk < lim && gq_dk2 + gq_dk3 < lim &&
+                       gg0 + gg1 + gg2 + gg3 < lim);
+    run_exact = __syncthreads_or(bad);
     // dgc total into shared memory (ring is idle after the last drain)
-    __syncthreads();
+    if (!run_exact) {
 #pragma unroll
     for (int qd = 0; qd < 4; ++qd) {
       const int c0 = cb + qd * 16;
@@ -648,42 +684,14 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             pg.w + san(dgr[qd * 16 + t + 3], p.clip));
       }
     }
-  } else {
-    // exact elementwise form (gdn2_bwd.py:298-328)
-    for (int e = threadIdx.x; e < C * D; e += kThreads) {
-      const int x = e / D, d = e % D;
-      const float kx = to_f<T>(kc[x * rs + d]), bx = to_f<T>(bc[x * rs + d]);
-      const float lq = p.scale * to_f<T>(qc[x * rs + d]), lk = bx * kx;
-      float dlq = 0.f, dlk = 0.f, drq = 0.f, drk = 0.f, dgi = 0.f, dgj = 0.f;
-      for (int y = 0; y < C; ++y) {
-        if (y <= x) {
-          const float dd = gc[x * GLD + d] - gc[y * GLD + d];
-          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
-          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
-          const float mq = dAqkT[y * C + x], mk = (y < x) ? dAkkT[y * C + x] : 0.f;
-          const float ry = to_f<T>(kc[y * rs + d]) * ed;
-          dlq = fmaf(mq, ry, dlq);
-          dlk = fmaf(mk, ry, dlk);
-          dgi += (mq * lq + mk * lk) * ry * cm;
-        }
-        if (y >= x) {
-          const float dd = gc[y * GLD + d] - gc[x * GLD + d];
-          const float ed = __expf(fminf(fmaxf(dd, -20.f), 20.f));
-          const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
-          const float mq = dAqkT[x * C + y], mk = (y > x) ? dAkkT[x * C + y] : 0.f;
-          const float lqy = p.scale * to_f<T>(qc[y * rs + d]) * ed;
-          const float lky = to_f<T>(bc[y * rs + d]) * to_f<T>(kc[y * rs + d]) * ed;
-          drq = fmaf(mq, lqy, drq);
-          drk = fmaf(mk, lky, drk);
-          dgj += (mq * lqy + mk * lky) * kx * cm;
-        }
-      }
-      dq_out[off + x * rs + d] = from_f<T>(san(pdq[e] + san(p.scale * dlq, p.clip), kFinalClipTc));
-      db_out[off + x * rs + d] = from_f<T>(san(pdb[e] + san(dlk * kx, p.clip), kFinalClipTc));
-      dk_out[off + x * rs + d] =
-          from_f<T>(san(pdk[e] + san(drq + drk + dlk * bx, p.clip), kFinalClipTc));
-      sdg[e] = pdgc[e] + san(dgi - dgj, p.clip);
     }
+    if (run_exact && threadIdx.x == 0) atomicOr(ws.status + 4, 1);
+  }
+  if (run_exact) {
+    // the reference's pair order: positive gates, wide gate spreads, BC < 32,
+    // or a chunk whose guard failed (its fast-path outputs are overwritten)
+    b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, GLD, dAqkT, dAkkT, pdq, pdk, pdb, pdgc, dq_out,
+                      dk_out, db_out, off, sdg, p.scale, p.clip);
   }
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);

@@ -41,6 +41,7 @@ constexpr int GLD = D + 4;   // row stride of the resident gc tile (conflict-fre
 constexpr int kIss = GDN2_FWD_ISS;
 
 struct TcSmemF {
+  float rowl1[C];   // sum_d |kg(i, d)| per row i
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
@@ -81,6 +82,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   float* tmp = S + TILE_FLOATS;                    // 4096 floats
 
   if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 512);
+  if (threadIdx.x < C) ts.rowl1[threadIdx.x] = 0.f;
   if (threadIdx.x == 0) {
     mbar_init(&ts.bars[0], kIss);
     mbar_init(&ts.bars[1], kIss);
@@ -133,10 +135,17 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       const int i = (wq & 31) * 4 + (l >> 3), d = ((wq >> 5) * 8 + (l & 7)) * 4;
       const float4 kv = ld4<T>(kc + i * rs + d), qv = ld4<T>(qc + i * rs + d);
       const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(gl + d);
-      sts4(kgo + i * D + d, make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
-                                        san(kv.y * __expf(l4.y - gi.y), p.clip),
-                                        san(kv.z * __expf(l4.z - gi.z), p.clip),
-                                        san(kv.w * __expf(l4.w - gi.w), p.clip)));
+      const float4 kg4 = make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
+                                     san(kv.y * __expf(l4.y - gi.y), p.clip),
+                                     san(kv.z * __expf(l4.z - gi.z), p.clip),
+                                     san(kv.w * __expf(l4.w - gi.w), p.clip));
+      sts4(kgo + i * D + d, kg4);
+      // row L1 norm of kg: the 8 lanes sharing row i cover 32 columns
+      float l1 = fabsf(kg4.x) + fabsf(kg4.y) + fabsf(kg4.z) + fabsf(kg4.w);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+      if ((l & 7) == 0) atomicAdd(&ts.rowl1[i], l1);
       tq[(d + 0) * QLD + i] = san(qv.x * __expf(gi.x), p.clip);
       tq[(d + 1) * QLD + i] = san(qv.y * __expf(gi.y), p.clip);
       tq[(d + 2) * QLD + i] = san(qv.z * __expf(gi.z), p.clip);
@@ -150,6 +159,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       qgo[e] = tq[(e >> 7) * QLD + (e & 127)];
     }
     __syncthreads();
+    // max_i ||kg_i||_1, the gain of dv_new's kg dh term (backward guard)
+    const float kl1 = block_max(threadIdx.x < C ? ts.rowl1[threadIdx.x] : 0.f, red);
+    if (threadIdx.x == 0) ws.bnd[chunk * 4] = kl1;
   }
 
   GDN2_TMARK(1);
@@ -274,7 +286,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 
   GDN2_TMARK(3);
   // ---- phase 2: A = (I + Akk)^-1 on the transpose (gdn2_fwd.py:173-260)
-  wy_inverse_T128(S, TLD, tmp, t0, p.clip);
+  wy_inverse_T128(S, TLD, tmp, t0, p.bc, p.clip);
   GDN2_TMARK(4);
   float* at = ws.AT + chunk * C * C;
   for_tile([&](int j, int i) { sts4(at + j * C + i, lds4(S + j * TLD + i)); });

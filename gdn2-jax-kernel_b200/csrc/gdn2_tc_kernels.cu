@@ -21,6 +21,7 @@ using namespace tc;
 namespace {
 
 struct TcSmem {
+  float red[8];
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
 constexpr int kScanSlots = 10;
 constexpr int kScanSliceBytes = SLICE_FLOATS * 4;   // one plane of one slice
 struct ScanSmem {
+  float wmax[2][8];   // per-warp max |state|, double-buffered by step parity
   uint64_t full[kScanSlots];
   uint64_t done;
   uint32_t tmem;
@@ -186,6 +188,16 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     float* hp = ws.hpre + (bh * p.nc) * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) hp[e] = src0 ? san(src0[e], p.clip) : 0.f;
   }
+  // Backward guard.  The affine step replaces the reference's
+  // dv_new = san(dv_partial + kg dh) by the unclipped sum, which is the same
+  // value while |dv_partial + kg dh| <= CLIP.  That holds whenever
+  // max|dv_partial| + max_i ||kg_i||_1 max|dh| < CLIP (ws.bnd); a (b, h) whose
+  // chain fails the test anywhere is flagged and recomputed by the exact
+  // reference step (k_bwd_state).  smax = this thread's max |state|.
+  constexpr bool kGuard = BWD && !PROD;
+  float smax = 0.f;
+  bool flagged = false;
+  bool clipped = false;   // the state sanitiser acted (reported for sequence parallelism)
 #pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     const int c0 = dcol0 + q * 16;
@@ -194,12 +206,20 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     for (int j = 0; j < 16; ++j) {
       const float x = PROD ? (vrow == c0 + j ? 1.f : 0.f)
                            : (src0 ? san(src0[(c0 + j) * D + vrow], p.clip) : 0.f);
+      smax = fmaxf(smax, fabsf(x));
       split(x, hv[j], lv[j]);
     }
     tmem_st16(lane_quarter_addr(tmem, 128 + c0), hv);
     tmem_st16(lane_quarter_addr(tmem, 256 + c0), lv);
   }
   tmem_st_wait();
+  auto publish_max = [&](int parity) {
+    float m = smax;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) ts.wmax[parity][warp] = m;
+  };
+  if (kGuard) publish_max(0);
 
   uint32_t ph = 0;
   float addv[64];
@@ -229,6 +249,16 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     fence_before_sync();
     __syncthreads();   // lo planes and the state in TMEM ready for the MMAs
     fence_after_sync();
+    if (kGuard) {
+      float m = ts.wmax[it & 1][0];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) m = fmaxf(m, ts.wmax[it & 1][w]);
+      float* bd = ws.bnd + chunk * 4;
+      // NaN anywhere fails the comparison and flags the chunk
+      const bool ok = bd[1] + bd[0] * m < p.clip * (1.f - 1e-5f);
+      flagged |= !ok;
+      if (threadIdx.x == 0) bd[2] = ok ? 0.f : 1.f;
+    }
     if (threadIdx.x == 0) {
       for (int s = 0; s < D / KS; ++s) {
         const int slot = (it * (D / KS) + s) % kScanSlots;
@@ -247,6 +277,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
         if (t < nt) issue(t);
       }
     const bool last = it == p.nc - 1;
+    smax = 0.f;
     float* dst;
     if (PROD) dst = last ? out_final + bh * D * D : nullptr;
     else if (!BWD) dst = last ? (out_final ? out_final + bh * D * D : nullptr) : ws.hpre + (chunk + 1) * D * D;
@@ -259,7 +290,10 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
       float hv[16], lv[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const float y = PROD ? x[j] : san(x[j] + addv[q * 16 + j], p.clip);
+        const float pre = x[j] + addv[q * 16 + j];
+        const float y = PROD ? x[j] : san(pre, p.clip);
+        if (!PROD && !(fabsf(pre) <= p.clip)) clipped = true;
+        if (kGuard) smax = fmaxf(smax, fabsf(y));
         if (dst) dst[(c0 + j) * D + vrow] = y;
         if (BWD && last && out_final) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y, 1e4f);
         split(y, hv[j], lv[j]);
@@ -268,7 +302,11 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
       tmem_st16(lane_quarter_addr(tmem, 256 + c0), lv);
     }
     tmem_st_wait();
+    if (kGuard) publish_max((it + 1) & 1);
   }
+  if (kGuard && threadIdx.x == 0) ws.bnd[bh * p.nc * 4 + 3] = flagged ? 1.f : 0.f;
+  if (clipped) atomicOr(ws.status + (BWD ? 2 : 1), 1);
+  if (kGuard && flagged && threadIdx.x == 0) atomicOr(ws.status + 3, 1);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -382,6 +420,7 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   // K = j) in shared memory, the B operand of -W^T dvp.
   float* dvp = ws.dvp + chunk * C * D;
   float* dt = sm;
+  float amax = 0.f;
   for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
     float* hi = dt + (c0 / KS) * 2 * SLICE_FLOATS;
 #pragma unroll
@@ -390,11 +429,15 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         y[t] = san(x[k + t], p.clip);
+        amax = fmaxf(amax, fabsf(y[t]));
         dvp[(c0 + k + t) * D + v] = y[t];
       }
       st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + k, KS, make_float4(y[0], y[1], y[2], y[3]));
     }
   });
+  // max |dv_partial|: the constant part of the backward guard
+  amax = block_max(amax, ts.red);
+  if (threadIdx.x == 0) ws.bnd[chunk * 4 + 1] = amax;
   const float* wt = ws.WT + chunk * C * D;
   ring.base = sm + 4 * 2 * SLICE_FLOATS;
   ring.nop = 1;
@@ -462,6 +505,11 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
   k_tc_scan<true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, dh_final, dh0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdScan, s);
+  // The (b, h) whose guard failed rerun the reference's three-product step
+  // (the CTAs of every other (b, h) return at once).
+  hook.begin(kStageBwdExact, s);
+  if ((e = launch_bwd_state<C, D>(p, ws, dout, dh_final, dh0, s, true)) != cudaSuccess) return e;
+  hook.end(kStageBwdExact, s);
   // dv_new is formed by the first product of k_tc_bwd_intra1
   return cudaSuccess;
 }

@@ -196,16 +196,29 @@ struct Src {
   long ld;
   float sc;
   bool trans;
+  float clip;   // > 0: the staged values are sanitised to +-clip (after scaling)
 };
-__device__ __forceinline__ Src direct(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, false}; }
-__device__ __forceinline__ Src trans(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, true}; }
+__device__ __forceinline__ Src direct(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, false, 0.f}; }
+__device__ __forceinline__ Src trans(const float* p, long ld, float sc = 1.f, float clip = 0.f) {
+  return Src{p, ld, sc, true, clip};
+}
 __device__ __forceinline__ void src_load(const Src& s, int k0, Frag& f) {
   if (s.trans) load_trans(f, s.p, s.ld, k0);
   else load_direct(f, s.p, s.ld, k0);
 }
 __device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, const Frag& f) {
-  if (s.trans) store_trans(hi, lo, f, s.sc);
-  else store_direct(hi, lo, f, s.sc);
+  Frag g = f;
+  if (s.clip > 0.f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      g.v[i] = make_float4(san(s.sc * f.v[i].x, s.clip), san(s.sc * f.v[i].y, s.clip),
+                           san(s.sc * f.v[i].z, s.clip), san(s.sc * f.v[i].w, s.clip));
+    if (s.trans) store_trans(hi, lo, g, 1.f);
+    else store_direct(hi, lo, g, 1.f);
+    return;
+  }
+  if (s.trans) store_trans(hi, lo, g, s.sc);
+  else store_direct(hi, lo, g, s.sc);
 }
 
 // K = 128 pass over NOP float32 sources with register double-buffering: the

@@ -11,6 +11,7 @@ namespace gdn2 {
 
 struct Problem {
   int B, T, H, D, C, nc;   // C = chunk length BT, nc = T / C
+  int bc;                  // the reference's sub-block BC (clip granularity of B4)
   float scale, clip;
   __host__ __device__ long row_stride() const { return (long)H * D; }
 };
@@ -45,15 +46,21 @@ struct Workspace {
                  //   [0, D^2): M as 4 K-slices, canonical 128 x 32 tiles (rows =
                  //   row of M, K = column); [D^2, 2 D^2): the same for M^T
   float* Bc;     // [D][D]  kg^T U
+  float* bnd;    // [4] per chunk, the exactness guard of the affine backward chain:
+                 //   [0] max_i sum_d |kg(i,d)|   (forward intra kernel)
+                 //   [1] max |dv_partial|        (backward prep kernel)
+                 //   [2] 1 if this chunk's step could clip dv_new (backward scan)
+                 //   [3] on the first chunk of each (b,h): 1 if any of its chunks could
   float* E;      // [D][D]  scale qg^T do - W^T dv_partial
   float* dvp;    // [C][D]  dv_partial = san(Aqk^T do)
-  int* status;   // device status word (1 = a bounded wait timed out); sticky
+  int* status;   // device status word (1 = a bounded wait timed out), zeroed by every entry point
   size_t bytes;
 
   static size_t per_chunk_floats(int C, int D, bool bwd) {
     size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + D;   // forward
     f += (size_t)D * D + (size_t)C * D;                        // residuals
     f += 3 * (size_t)D * D;                                    // M (both ways), Bc
+    f += 4;                                                    // bnd
     if (bwd) f += 2 * (size_t)C * C + 7 * (size_t)C * D + 2 * (size_t)D * D;
     return f;
   }
@@ -80,6 +87,7 @@ struct Workspace {
     w.vnew = take((size_t)C * D);
     w.M = take(2 * (size_t)D * D);
     w.Bc = take((size_t)D * D);
+    w.bnd = take(4);
     if (bwd) {
       w.dv = take((size_t)C * D);
       w.dh = take((size_t)D * D);

@@ -14,6 +14,9 @@ LIB_PATH = os.path.join(_HERE, "libgdn2.so")
 
 F32, BF16 = 0, 1
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA = 0, -1, -2, -3
+# bits of gdn2_workspace_status (include/gdn2.h)
+STATUS_WAIT_TIMEOUT, STATUS_FWD_STATE_CLIPPED, STATUS_BWD_STATE_CLIPPED = 1, 2, 4
+STATUS_EXACT_RECOMPUTE, STATUS_B4_EXACT = 8, 16
 ABI_VERSION = 1
 
 _lib = None
@@ -34,10 +37,13 @@ SIGNATURES = {
     "gdn2_selftest_gemm_tf32x3": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "gdn2_profile_read": (_i, [_i, ctypes.POINTER(ctypes.c_double),
                                ctypes.POINTER(ctypes.c_long), _i]),
+    "gdn2_workspace_status": (_i, [_vp, _sz, _vp]),
+    "gdn2_noalloc_status": (_i, [_vp]),
+    "gdn2_selftest_wait_timeout": (_i, [_vp, _sz, _i, _vp]),
 }
 
 STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3",
-          "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan")
+          "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan", "bwd_exact")
 
 
 def profile_enable(on=True):
@@ -55,6 +61,36 @@ def profile_read(reset=True):
 
 class Gdn2Error(RuntimeError):
     """A CUDA-side failure reported by libgdn2."""
+
+
+# When the device status word of a call is read back and checked:
+#   "sync"   at the points where the package synchronizes anyway (calls made
+#            with host tensors, whose results are copied back);
+#   "always" after every call (one stream synchronization per call);
+#   "never".
+# The environment variable GDN2_CHECK_STATUS sets the initial mode.
+CHECK_STATUS = os.environ.get("GDN2_CHECK_STATUS", "sync")
+LAST_STATUS = None   # status bits of the latest call that was checked
+
+
+def workspace_status(ws, stream):
+    """The status bits of the latest call on workspace tensor ``ws``
+    (STATUS_* above; 0 = nothing to report).  Synchronizes ``stream``."""
+    rc = load().gdn2_workspace_status(ws.data_ptr(), ws.numel(), stream)
+    if rc < 0:
+        check(rc, "gdn2_workspace_status")
+    return rc
+
+
+def check_status(ws, stream, what, synced):
+    """Raise Gdn2Error if the call that used ``ws`` recorded a timed-out wait.
+    ``synced``: the caller synchronizes at this point anyway."""
+    global LAST_STATUS
+    if CHECK_STATUS == "always" or (CHECK_STATUS == "sync" and synced):
+        LAST_STATUS = workspace_status(ws, stream)
+        if LAST_STATUS & STATUS_WAIT_TIMEOUT:
+            raise Gdn2Error(f"{what}: a bounded barrier wait inside a kernel timed out; "
+                            "the results of this call are invalid")
 
 
 def load():

@@ -47,6 +47,7 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
         db.data_ptr(), dg.data_ptr(), dh0.data_ptr(), ws.data_ptr(), ws.numel(),
         int(residuals_valid), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip, p.stream)
     _lib.check(rc, "gdn2_bwd")
+    _lib.check_status(ws, p.stream, "gdn2_bwd", synced=p.on_host)
     out = [p.unpad(t) for t in (dq, dk, dv, dw, db, dg)]
     order = (0, 1, 2, 3, 4, 5)  # q k v w b g
     out = [t.to(p.in_dtypes[i]) for t, i in zip(out, order)]

@@ -29,8 +29,8 @@ BC = 128     # sub-block length (the reference's clip granularity; results do no
 MB = 16      # micro-block of the triangular solve
 CLIP = 1e4   # stage sanitiser bound
 # Chunk length policy.  EXACT_BT = True (default) runs chunks of BT itself
-# (split into 128 or 64 when BT is larger), which reproduces the reference
-# bit for bit in where its clips act.  EXACT_BT = False lets a head dim of
+# (split into 128 or 64 when BT is larger); with BT = 128 or 64 this places
+# every clip where the reference places it.  EXACT_BT = False lets a head dim of
 # 128 run chunks of 128 (the tensor-core kernels) whenever T allows, whatever
 # BT says: the chunked form is exact for any chunk length, so results agree
 # to float32 rounding unless a gate is positive and the +-20 exponent clip or
@@ -107,7 +107,14 @@ class _Prepared:
         bc = int(BC)
         if bc <= 0 or self.bt_user % bc != 0:
             raise Gdn2ShapeError(f"BC={bc} must divide BT={self.bt_user}")
+        if bc % MB:
+            raise Gdn2ShapeError(f"BC={bc} must be a multiple of MB={MB} (gdn2_fwd.py:194)")
+        # BC places the sanitisers of the WY solve and of B4's accumulators.
+        # Chunks merged beyond BT (EXACT_BT = False) already move them, and
+        # run with sub-blocks of 64, the tensor-core kernels' fast layout.
         self.bc = bc if self.C % bc == 0 else self.C
+        if self.C > self.bt_user:
+            self.bc = 64
         if any(not t.dtype.is_floating_point for t in ts):
             raise Gdn2ShapeError("inputs must be floating point")
         if h0 is not None and tuple(torch.as_tensor(h0).shape) != (B, H, D, D):
@@ -166,6 +173,7 @@ def _run_forward(p, save_residuals=False, ws=None):
                       int(save_residuals), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip,
                       p.stream)
     _lib.check(rc, "gdn2_fwd")
+    _lib.check_status(ws, p.stream, "gdn2_fwd", synced=p.on_host)
     return p.unpad(o), h_final, ws
 
 

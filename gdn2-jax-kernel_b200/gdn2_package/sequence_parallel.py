@@ -17,6 +17,16 @@ sequence (gdn2_fwd.py:362, gdn2_bwd.py:77); here:
             ranks exchange e, compose their incoming gradient and run the
             ordinary backward of their segment with it.
 
+Exactness.  The reference sanitises the state after every chunk (h and dh
+clipped to +-CLIP, gdn2_fwd.py:358, gdn2_bwd.py:73) and dv_new inside the
+backward chain (gdn2_bwd.py:68).  A clip that acts makes a segment's map
+non-affine, so the composed start states (and gradients) are exact only while
+no sanitiser acts on the chain.  The kernels report every such event in the
+workspace status (STATUS_*_STATE_CLIPPED, STATUS_EXACT_RECOMPUTE); the ranks
+exchange these bits and raise Gdn2SaturationError instead of returning
+inexact results.  Within one rank (and in the non-parallel entry points) the
+sanitisers are applied exactly.
+
 Only these D x D boundary tiles cross the interconnect.  The exchange is one
 all-gather through `torch.distributed` (NCCL over NVLink on B200 nodes); a
 custom `gather(list_of_tensors) -> list_per_rank` can replace it, which is how
@@ -28,6 +38,33 @@ import torch
 
 from . import _lib
 from . import gdn2_fwd as _fwd
+
+
+class Gdn2SaturationError(_lib.Gdn2Error):
+    """A state sanitiser acted inside a segment, so the affine composition of
+    the segments would not equal the reference's serial scan."""
+
+
+def _status(p, ws):
+    return _lib.workspace_status(ws, p.stream)
+
+
+def _check_linear(bits, p, gather, what):
+    """All ranks share their status bits; raise if any rank saw a clip that
+    breaks the segment maps, or a timed-out wait."""
+    t = torch.tensor([bits], dtype=torch.int32, device=p.dev)
+    allbits = 0
+    for x in gather(t):
+        allbits |= int(x.item())
+    if allbits & _lib.STATUS_WAIT_TIMEOUT:
+        raise _lib.Gdn2Error(f"{what}: a bounded barrier wait inside a kernel timed out")
+    bad = _lib.STATUS_FWD_STATE_CLIPPED if what == "sp_forward" else \
+        (_lib.STATUS_BWD_STATE_CLIPPED | _lib.STATUS_EXACT_RECOMPUTE)
+    if allbits & bad:
+        raise Gdn2SaturationError(
+            f"{what}: the CLIP sanitiser acted on the recurrence inside a segment "
+            f"(status bits {allbits:#x}); the sequence-parallel composition is exact only "
+            "while it does not; run this input without sequence parallelism")
 
 
 def compose_forward(maps, consts, h0):
@@ -89,10 +126,12 @@ def sp_forward_local(q, k, v, w, b, g, scale, rank):
         raise _fwd.Gdn2ShapeError("sequence parallelism needs segments divisible by BT")
     ws = p.workspace(True)
     o, c_seg, _ = _fwd._run_forward(p, save_residuals=True, ws=ws)
+    bits = _status(p, ws)
     P = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
     _seg(0, ws, p, None, None, P)
     st = SegmentState(p, ws, None, rank, None)
     st.o = o
+    st.bits = bits
     return st, P, c_seg
 
 
@@ -107,6 +146,7 @@ def sp_forward_finish(state, maps, consts, h0=None):
     state.h_start = starts[state.rank].float().contiguous()
     h_end = torch.empty_like(state.h_start)
     _seg(1, state.ws, p, state.h_start, state.o, h_end)
+    state.bits |= _status(p, state.ws)
     return state.o, final.float()
 
 
@@ -116,6 +156,7 @@ def sp_backward_local(state, dout):
     state.do = torch.as_tensor(dout).to(p.dev, torch.float32).contiguous()
     e = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
     _seg(2, state.ws, p, state.do, None, e)
+    state.bwd_bits = _status(p, state.ws)
     return e
 
 
@@ -129,6 +170,7 @@ def sp_backward_finish(state, terms, dh_final=None):
     g_in, g0 = compose_backward(state.maps, terms, dhf)
     g_rank = g_in[state.rank].float().contiguous()
     grads = _bwd.gdn2_backward(*p.t, p.scale, state.h_start, state.do, g_rank, workspace=state.ws)
+    state.bwd_bits |= _status(p, state.ws)
     grads = [t.to(dt) for t, dt in zip(grads[:6], p.in_dtypes)]
     dh0 = torch.nan_to_num(g0.clamp(-1e4, 1e4), nan=0.0).float()
     return (*grads, dh0)
@@ -140,6 +182,7 @@ def sp_forward(q, k, v, w, b, g, scale, h0=None, rank=0, gather=None):
     gather = gather or dist_gather()
     st, P, c = sp_forward_local(q, k, v, w, b, g, scale, rank)
     o, hf = sp_forward_finish(st, gather(P), gather(c), h0)
+    _check_linear(st.bits, st.p, gather, "sp_forward")
     return o, hf, st
 
 
@@ -147,7 +190,9 @@ def sp_backward(state, dout, dh_final, gather=None):
     """Backward of this rank's segment; dh0 is the same on every rank."""
     gather = gather or dist_gather()
     e = sp_backward_local(state, dout)
-    return sp_backward_finish(state, gather(e), dh_final)
+    out = sp_backward_finish(state, gather(e), dh_final)
+    _check_linear(state.bwd_bits, state.p, gather, "sp_backward")
+    return out
 
 
 class _SPCore(torch.autograd.Function):

@@ -43,3 +43,28 @@ def make_inputs(B, T, H, D, seed=0, h0_std=None, grads=True, dtype=np.float32):
     out = {n: a.astype(dtype) for n, a in out.items()}
     out["scale"] = float(1.0 / np.sqrt(D))
     return out
+
+
+def make_inputs_torch(B, T, H, D, seed=0, device="cuda", h0_std=None, grads=True):
+    """The same distributions drawn by torch on ``device`` (float32), for
+    benchmark sizes whose host-side generation would take minutes.  The values
+    are not bit-identical to ``make_inputs``."""
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    shape = (B, T, H, D)
+
+    def nrm(s):
+        return torch.randn(s, generator=gen, device=device, dtype=torch.float32)
+
+    q = torch.nn.functional.normalize(nrm(shape), dim=-1)
+    k = torch.nn.functional.normalize(nrm(shape), dim=-1)
+    out = dict(q=q, k=k, v=nrm(shape), w=torch.sigmoid(nrm(shape)), b=torch.sigmoid(nrm(shape)),
+               g=-torch.nn.functional.softplus(nrm(shape)))
+    if h0_std is not None:
+        out["h0"] = h0_std * nrm((B, H, D, D))
+    if grads:
+        out["dout"] = nrm(shape)
+        out["dh_final"] = nrm((B, H, D, D))
+    out["scale"] = float(D ** -0.5)
+    return out

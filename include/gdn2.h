@@ -14,9 +14,11 @@
  *   dh_final                (B, H, D, D) float32 cotangent of h_final
  *   dq, dk, dv, dw, db, dg  (B, T, H, D) in the input dtype (gdn2_pipeline.py:129-134)
  *   dh0                     (B, H, D, D) float32
- * BT is the chunk length (64 or 128), BC the reference's sub-block (any
- * divisor of BT; results do not depend on it), D the head dim (64 or 128),
- * clip the stage sanitiser bound CLIP (gdn2_fwd.py:33, 42-44).
+ * BT is the chunk length (64 or 128), BC the reference's sub-block (a
+ * multiple of MB = 16 dividing BT; it sets where the sanitisers of the WY
+ * solve and of B4's accumulators act, so results depend on it only when CLIP
+ * acts), D the head dim (64 or 128), clip the stage sanitiser bound CLIP
+ * (gdn2_fwd.py:33, 42-44).
  */
 #ifndef GDN2_H_
 #define GDN2_H_
@@ -82,6 +84,32 @@ int gdn2_sp_segment(int op, void* workspace, size_t workspace_bytes, const float
                     float* out, int B, int T, int H, int D, int BT, int BC, float scale,
                     float clip, void* stream);
 
+/* Device status of the latest call on a workspace (no counterpart in the
+ * reference, whose kernels have no device-side waits).  Every entry point
+ * that takes a workspace clears its status header on `stream` before its
+ * kernels run.  This call copies the header to the host, synchronizes
+ * `stream` and returns a bit set, or a negative GDN2_ERR_* code:
+ *   GDN2_STATUS_WAIT_TIMEOUT       a bounded barrier wait inside a kernel ran
+ *                                  out of polls; the call's outputs are invalid;
+ *   GDN2_STATUS_FWD_STATE_CLIPPED  the CLIP sanitiser acted on the state h in
+ *                                  the tensor-core scan (exact for a whole
+ *                                  sequence; breaks the linear segment maps of
+ *                                  gdn2_sp_segment);
+ *   GDN2_STATUS_BWD_STATE_CLIPPED  the same for the state gradient dh;
+ *   GDN2_STATUS_EXACT_RECOMPUTE    some (b, h) could clip dv_new inside the
+ *                                  backward chain and were recomputed with the
+ *                                  reference's exact step (breaks the segment
+ *                                  maps of gdn2_sp_segment; otherwise information);
+ *   GDN2_STATUS_B4_EXACT           some chunk's B4 accumulators could reach CLIP
+ *                                  and it ran the reference's sub-block pair
+ *                                  order (information only). */
+#define GDN2_STATUS_WAIT_TIMEOUT 1
+#define GDN2_STATUS_FWD_STATE_CLIPPED 2
+#define GDN2_STATUS_BWD_STATE_CLIPPED 4
+#define GDN2_STATUS_EXACT_RECOMPUTE 8
+#define GDN2_STATUS_B4_EXACT 16
+int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* stream);
+
 /* Forward for callers that cannot allocate device memory (no counterpart in
  * the reference).  Same arguments and results as gdn2_fwd without the
  * workspace: the scratch lives in a fixed device array of
@@ -97,6 +125,9 @@ int gdn2_fwd_noalloc(int dtype, const void* q, const void* k, const void* v, con
                      const void* b, const void* g, const float* h0, float* o, float* h_final,
                      int B, int T, int H, int D, int BT, int BC, float scale, float clip,
                      void* stream);
+/* gdn2_workspace_status() of the built-in scratch array on the current device:
+ * the status of the latest gdn2_fwd_noalloc call there (synchronizes `stream`). */
+int gdn2_noalloc_status(void* stream);
 
 /* Token-by-token decode of a short segment (B, T, H, D), carrying the state
  * h0 (B,H,D,D, may be NULL = zero) to h_final: the recurrence of
@@ -114,7 +145,7 @@ int gdn2_decode(int dtype, const void* q, const void* k, const void* v, const vo
  * recorded events and fills, per stage, the accumulated milliseconds and the
  * launch count (stages: 0 fwd_intra, 1 fwd_state, 2 bwd_state, 3 bwd_intra1,
  * 4 bwd_intra2, 5 bwd_intra3, 6 fwd_affine, 7 fwd_scan, 8 fwd_out, 9 bwd_prep,
- * 10 bwd_scan); it returns the number of stages. */
+ * 10 bwd_scan, 11 bwd_exact); it returns the number of stages. */
 int gdn2_profile_enable(int on);
 int gdn2_profile_read(int n, double* total_ms, long* launches, int reset);
 
@@ -126,6 +157,13 @@ int gdn2_profile_read(int n, double* total_ms, long* launches, int reset);
  * barrier wait timed out. */
 int gdn2_selftest_gemm_tf32x3(const float* A, const float* B, float* D, int batch, int K, int N,
                               int trans_a, int trans_b, int* status, void* stream);
+
+/* Self-test of the failure path (no counterpart in the reference): clears the
+ * status header of `workspace`, then one warp waits on a barrier that nothing
+ * completes, giving up after `polls` polls.  The wait records its timeout in
+ * the status word (read it with gdn2_workspace_status) and the kernel returns;
+ * nothing else is in flight, so the context stays usable. */
+int gdn2_selftest_wait_timeout(void* workspace, size_t workspace_bytes, int polls, void* stream);
 
 #ifdef __cplusplus
 }

@@ -56,7 +56,7 @@ def _load_reference(ref_dir, BT, BC, clip):
     return fwd, bwd, pipe
 
 
-def run_case(ref_dir, name, B, T, H, D, BT, BC, clip, seed, h0_std, ones=False):
+def run_case(ref_dir, name, B, T, H, D, BT, BC, clip, seed, h0_std, ones=False, dscale=1.0):
     sys.path.insert(0, os.path.join(HERE, "..", "..", "gdn2-jax-kernel_b200"))
     from gdn2_package.synthetic import make_inputs
 
@@ -66,6 +66,9 @@ def run_case(ref_dir, name, B, T, H, D, BT, BC, clip, seed, h0_std, ones=False):
         for n in ("q", "k", "v", "w", "b", "g"):
             inp[n] = np.ones_like(inp[n])
         inp["scale"] = 0.1
+    # upstream gradients scaled so that the clip acts inside the backward chain
+    inp["dout"] = (inp["dout"] * dscale).astype(np.float32)
+    inp["dh_final"] = (inp["dh_final"] * dscale).astype(np.float32)
     f64 = lambda a: np.asarray(a, dtype=np.float64)
     q, k, v, w, b, g = (f64(inp[n]) for n in ("q", "k", "v", "w", "b", "g"))
     h0 = f64(inp["h0"]) if "h0" in inp else np.zeros((B, H, D, D))
@@ -89,15 +92,20 @@ def run_case(ref_dir, name, B, T, H, D, BT, BC, clip, seed, h0_std, ones=False):
 
 
 CASES = [
-    # name, B, T, H, D, BT, BC, clip, seed, h0_std, ones
-    ("ref_bt64_bc32", 1, 128, 1, 128, 64, 32, 1e4, 1, 0.1, False),
-    ("ref_bt128_bc64", 1, 256, 1, 128, 128, 64, 1e3, 2, None, False),
-    ("ref_ones_bt64_bc32", 1, 128, 1, 128, 64, 32, 1e4, 3, None, True),
+    # name, B, T, H, D, BT, BC, clip, seed, h0_std, ones, dout scale
+    ("ref_bt64_bc32", 1, 128, 1, 128, 64, 32, 1e4, 1, 0.1, False, 1.0),
+    ("ref_bt128_bc64", 1, 256, 1, 128, 128, 64, 1e3, 2, None, False, 1.0),
+    ("ref_ones_bt64_bc32", 1, 128, 1, 128, 64, 32, 1e4, 3, None, True, 1.0),
+    # CLIP = 20 with dout, dh_final x 30: dv_new = san(dv_partial + kg dh)
+    # clips inside the backward state chain (gdn2_bwd.py:66-68), h and dh do not
+    ("ref_clip_bt128_bc64", 1, 512, 1, 128, 128, 64, 20.0, 4, 0.1, False, 30.0),
 ]
 
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GDN2_REFERENCE_DIR")
     if not ref:
         sys.exit("usage: make_golden.py <reference checkout>")
+    only = sys.argv[2:]   # optional case names
     for c in CASES:
-        run_case(ref, *c[:-1], ones=c[-1])
+        if not only or c[0] in only:
+            run_case(ref, *c[:-2], ones=c[-2], dscale=c[-1])

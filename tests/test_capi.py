@@ -32,7 +32,7 @@ def test_workspace_bytes():
     lib = _lib.load()
     B, T, H, D, C = 8, 8192, 6, 128, 128
     nc = T // C
-    fwd = (2 * C * C + 5 * C * D + D + 4 * D * D + C * D) * 4 * B * H * nc + 512
+    fwd = (2 * C * C + 5 * C * D + D + 4 * D * D + C * D + 4) * 4 * B * H * nc + 512
     bwd = fwd + (2 * C * C + 7 * C * D + 2 * D * D) * 4 * B * H * nc
     assert lib.gdn2_workspace_bytes(B, T, H, D, C, 0) == fwd
     assert lib.gdn2_workspace_bytes(B, T, H, D, C, 1) == bwd
@@ -51,7 +51,8 @@ def _fwd(**kw):
 
 @pytest.mark.parametrize("kw,frag", [
     (dict(D=96), "head dim"), (dict(BT=32), "chunk BT"), (dict(T=100), "divisible"),
-    (dict(BC=48), "sub-block"), (dict(dtype=7), "dtype"), (dict(clip=0.0), "clip"),
+    (dict(BC=48), "sub-block"), (dict(BC=8), "multiple of MB"), (dict(dtype=7), "dtype"),
+    (dict(clip=0.0), "clip"),
     (dict(B=0), "empty"),
 ])
 def test_invalid_arguments_rejected(kw, frag):
@@ -74,3 +75,38 @@ def test_python_api_shape_errors_match_reference_assertions():
     y = torch.zeros(1, 128, 2, 96)
     with pytest.raises(ValueError, match="head dim"):
         gdn2_pallas_forward(y, y, y, y, y, y, 0.1)
+
+
+def test_status_bits_match_header():
+    src = open(os.path.join(ROOT, "include", "gdn2.h")).read()
+    bits = dict(re.findall(r"#define GDN2_STATUS_(\w+) (\d+)", src))
+    assert int(bits["WAIT_TIMEOUT"]) == _lib.STATUS_WAIT_TIMEOUT
+    assert int(bits["FWD_STATE_CLIPPED"]) == _lib.STATUS_FWD_STATE_CLIPPED
+    assert int(bits["BWD_STATE_CLIPPED"]) == _lib.STATUS_BWD_STATE_CLIPPED
+    assert int(bits["EXACT_RECOMPUTE"]) == _lib.STATUS_EXACT_RECOMPUTE
+    assert int(bits["B4_EXACT"]) == _lib.STATUS_B4_EXACT
+
+
+def test_status_query_rejects_bad_workspace_without_gpu_work():
+    lib = _lib.load()
+    assert lib.gdn2_workspace_status(None, 1 << 20, None) == _lib.ERR_INVALID
+    assert lib.gdn2_workspace_status(ctypes.c_void_p(256), 16, None) == _lib.ERR_INVALID
+    assert lib.gdn2_selftest_wait_timeout(None, 1 << 20, 16, None) == _lib.ERR_INVALID
+
+
+def test_check_status_modes(monkeypatch):
+    """The Python layer reads the status word only where its mode says, and a
+    timed-out wait raises Gdn2Error (the read itself faked: no GPU here)."""
+    seen = []
+    monkeypatch.setattr(_lib, "workspace_status", lambda ws, s: seen.append(1) or 1)
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "sync")
+    _lib.check_status(None, None, "x", synced=False)
+    assert not seen
+    with pytest.raises(_lib.Gdn2Error, match="timed out"):
+        _lib.check_status(None, None, "x", synced=True)
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "never")
+    _lib.check_status(None, None, "x", synced=True)
+    assert len(seen) == 1
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
+    with pytest.raises(_lib.Gdn2Error):
+        _lib.check_status(None, None, "x", synced=False)

@@ -129,9 +129,15 @@ def test_masked_tail(D, BT, BC):
         assert a.shape == b.shape and rel(a, b) < 1e-4, (name, rel(a, b))
 
 
-@pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64"])
-def test_against_reference_golden(name):
-    """Outputs of the reference source itself (tests/golden/make_golden.py)."""
+@pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64", "ref_clip_bt128_bc64"])
+def test_against_reference_golden(name, monkeypatch):
+    """Outputs of the reference source itself (tests/golden/make_golden.py).
+    ref_clip_bt128_bc64 runs CLIP = 20 with dout, dh_final x 30, so that
+    dv_new = san(dv_partial + kg dh) clips inside the backward state chain
+    (gdn2_bwd.py:66-68): the tensor-core backward must flag those (b, h) and
+    recompute them with the exact step."""
+    from gdn2_package import _lib
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
     z = np.load(os.path.join(GOLDEN, name + ".npz"))
     B, T, H, D, BT, BC = (int(x) for x in z["meta"])
     _set_consts(BT, BC, float(z["clip"]))
@@ -141,8 +147,74 @@ def test_against_reference_golden(name):
     assert rel(o, z["o"]) < 1e-4 and rel(h, z["h_final"]) < 1e-4
     grads = gdn2_backward(*args, float(z["scale"]), h0, torch.as_tensor(z["dout"]).cuda(),
                           torch.as_tensor(z["dh_final"]).cuda())
+    if name == "ref_clip_bt128_bc64":
+        assert _lib.LAST_STATUS & _lib.STATUS_EXACT_RECOMPUTE
     for gname, a in zip(GRADS, grads):
         assert rel(a, z[gname]) < 1e-4, (gname, rel(a, z[gname]))
+
+
+@pytest.mark.parametrize("clip,dscale,h0s,gscale", [
+    (20.0, 30.0, 0.1, 1.0),    # dv_new clips inside the backward chain, B4 accumulators clip
+    (0.3, 1.0, 0.1, 1.0),      # U, W, kg, o and the backward clip
+    (0.5, 1.0, 0.1, 0.01),     # slow gates: the forward state h itself clips
+    (1e3, 1.0, None, 1.0),     # nothing clips: the fast paths run, no recompute
+])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("BT,BC", [(128, 64), (64, 16)])
+def test_backward_with_clip_active(BT, BC, clip, dscale, h0s, gscale, dtype, monkeypatch):
+    """The CLIP sanitiser acting, against the float64 oracle: o, h_final and
+    all seven gradients.  BT = D = 128 runs the tcgen05 kernels (affine chain
+    with its guard, B4 guard), BT = 64 the CUDA-core kernels (B4 guard)."""
+    from gdn2_package import _lib
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
+    _set_consts(BT, BC, clip)
+    inp = make_inputs(2, 768, 2, 128, seed=31, h0_std=h0s)
+    inp["g"] = inp["g"] * np.float32(gscale)
+    inp["dout"] = inp["dout"] * np.float32(dscale)
+    inp["dh_final"] = inp["dh_final"] * np.float32(dscale)
+    args = _dev(inp, dtype)
+    h0 = torch.as_tensor(inp["h0"]).cuda() if "h0" in inp else None
+    o, h = gdn2_pallas_forward(*args, inp["scale"], h0)
+    ref_in = _rounded(inp, dtype)
+    o_r, h_r = O.forward(*ref_in, inp["scale"], inp.get("h0"), BT, BC, clip)
+    tol = TOL[dtype]
+    assert rel(o, o_r) < tol and rel(h, h_r) < tol, (rel(o, o_r), rel(h, h_r))
+    grads = gdn2_backward(*args, inp["scale"], h0, torch.as_tensor(inp["dout"]).cuda(),
+                          torch.as_tensor(inp["dh_final"]).cuda())
+    if BT == 128:
+        recomputed = bool(_lib.LAST_STATUS & _lib.STATUS_EXACT_RECOMPUTE)
+        assert recomputed == (clip < 1e3), _lib.LAST_STATUS
+    if clip >= 1e3:
+        assert not _lib.LAST_STATUS & _lib.STATUS_B4_EXACT, _lib.LAST_STATUS
+    g_r = O.backward(*ref_in, inp["scale"], inp.get("h0"), inp["dout"], inp["dh_final"], BT, BC,
+                     clip)
+    for name, a, b in zip(GRADS, grads, g_r):
+        assert rel(a, b) < tol, (name, rel(a, b))
+
+
+def test_wait_timeout_surfaces_and_context_survives(monkeypatch):
+    """A kernel whose barrier wait runs out records it in the workspace status
+    and returns; the Python layer raises Gdn2Error; the next call clears the
+    word and the CUDA context keeps working."""
+    from gdn2_package import _lib
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
+    assert lib.gdn2_selftest_wait_timeout(ws.data_ptr(), ws.numel(), 256, stream) == 0
+    assert _lib.workspace_status(ws, stream) == _lib.STATUS_WAIT_TIMEOUT
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
+    with pytest.raises(_lib.Gdn2Error, match="timed out"):
+        _lib.check_status(ws, stream, "selftest", synced=False)
+    # a real call on a workspace whose word was set starts from a clear word
+    _set_consts(128, 64, 1e4)
+    inp = make_inputs(1, 256, 1, 128, seed=2, grads=False)
+    from gdn2_package.gdn2_fwd import _Prepared, _run_forward
+    p = _Prepared(*_dev(inp, torch.float32), inp["scale"], None)
+    big = p.workspace(False)
+    assert lib.gdn2_selftest_wait_timeout(big.data_ptr(), big.numel(), 64, stream) == 0
+    o, h, _ = _run_forward(p, ws=big)
+    assert _lib.LAST_STATUS == 0
+    assert torch.isfinite(o).all() and float((torch.ones(4, device="cuda") * 2).sum()) == 8.0
 
 
 def test_against_reference_golden_saturated():
@@ -152,9 +224,17 @@ def test_against_reference_golden_saturated():
     B, T, H, D, BT, BC = (int(x) for x in z["meta"])
     _set_consts(BT, BC, float(z["clip"]))
     args = [torch.as_tensor(z[n]).cuda() for n in NAMES]
-    o, h = gdn2_pallas_forward(*args, float(z["scale"]), torch.as_tensor(z["h0"]).cuda())
+    h0 = torch.as_tensor(z["h0"]).cuda()
+    o, h = gdn2_pallas_forward(*args, float(z["scale"]), h0)
     assert rel(o, z["o"]) < 1e-4 and rel(h, z["h_final"]) < 1e-4
     assert o.shape == (B, T, H, D) and h.shape == (B, H, D, D)
+    # dk and dg are cancellation noise scaled by e^63 here (sign depends on
+    # summation order): the remaining gradients are compared
+    grads = dict(zip(GRADS, gdn2_backward(*args, float(z["scale"]), h0,
+                                          torch.as_tensor(z["dout"]).cuda(),
+                                          torch.as_tensor(z["dh_final"]).cuda())))
+    for gname in ("dq", "dv", "dw", "db", "dh0"):
+        assert rel(grads[gname], z[gname]) < 1e-4, (gname, rel(grads[gname], z[gname]))
 
 
 def test_reference_shape_tests_on_gpu():

@@ -50,4 +50,13 @@ def test_bench_tables_cover_every_profiled_stage():
     fl, by = bench.flops_per_chunk(128, 128), bench.bytes_per_chunk(128, 128)
     assert set(_lib.STAGES) == set(fl) == set(by)
     assert set(bench.NCU_TRAFFIC_PER_CHUNK) <= set(_lib.STAGES)
-    assert all(v > 0 for v in fl.values()) and all(v > 0 for v in by.values())
+    work = {k for k in fl if k != "bwd_exact"}   # the guard launch does no work unless flagged
+    assert all(fl[k] > 0 for k in work) and all(by[k] > 0 for k in work)
+    assert fl["bwd_exact"] == 0 and by["bwd_exact"] == 0
+    # step-level work: the benchmark spec's per token and head figures for config 1
+    f, b = bench.step_work(bench.CONFIGS[1])
+    assert abs(f - 2.19e11) / 2.19e11 < 0.01 and abs(b - 4.03e9) / 4.03e9 < 0.01
+    assert bench.tensor_peak(bench.CONFIGS[1], 1659.4)[0] == 1659.4 / 6
+    assert bench._shard(bench.CONFIGS[1], 8, 0, "strong") == (1, 6)
+    assert bench._shard(bench.CONFIGS[1], 4, 0, "strong") == (2, 6)
+    assert bench._shard(bench.CONFIGS[1], 8, 0, "weak") == (8, 6)

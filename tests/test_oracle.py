@@ -32,7 +32,7 @@ def _golden(name):
     return z, BT, BC, float(z["clip"]), float(z["scale"])
 
 
-@pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64"])
+@pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_bt128_bc64", "ref_clip_bt128_bc64"])
 def test_oracle_matches_reference_golden(name):
     z, BT, BC, clip, scale = _golden(name)
     args = [z[n].astype(np.float64) for n in NAMES]

@@ -112,6 +112,33 @@ def test_sp_emulated_matches_full_sequence(R):
     assert _rel(grads[0][6], g_ref[6]) < 1e-4
 
 
+@pytest.mark.gpu
+@pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")
+def test_sp_reports_saturation():
+    """A CLIP that acts on the state inside a segment makes the segment map
+    non-affine: the ranks see it in the status bits and raise instead of
+    returning a composition that differs from the serial scan."""
+    from gdn2_package import gdn2_fwd
+    gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP = 128, 64, 0.5
+    R, B, T, H = 2, 1, 512, 1
+    inp = _inputs(B, T, H, 6)
+    inp["g"] = inp["g"] * 0.01   # slow decay: the state grows past CLIP = 0.5
+    x = [torch.as_tensor(inp[n]).cuda() for n in NAMES]
+    L = T // R
+    seg = lambda t, r: t[:, r * L:(r + 1) * L].contiguous()
+    states, Ps, cs = [], [], []
+    for r in range(R):
+        st, P, c = SP.sp_forward_local(*[seg(t, r) for t in x], inp["scale"], r)
+        states.append(st); Ps.append(P); cs.append(c)
+    for st in states:
+        SP.sp_forward_finish(st, Ps, cs, None)
+    bits = [st.bits for st in states]
+    assert any(b & SP._lib.STATUS_FWD_STATE_CLIPPED for b in bits), bits
+    emulated = lambda t: [torch.tensor([b], dtype=torch.int32) for b in bits]
+    with pytest.raises(SP.Gdn2SaturationError):
+        SP._check_linear(bits[0], states[0].p, emulated, "sp_forward")
+
+
 _NCCL_WORKER = r'''
 import os, sys, torch, torch.distributed as dist
 sys.path.insert(0, os.path.join(sys.argv[1], "gdn2-jax-kernel_b200"))

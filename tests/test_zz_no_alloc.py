@@ -53,3 +53,5 @@ def test_noalloc_matches_workspace_forward_twice(B, T, H, D, BT, BC):
         assert rc == 0, lib.gdn2_last_error()
         torch.cuda.synchronize()
         assert _rel(o, o_ref) < 1e-4 and _rel(h, h_ref) < 1e-4, call
+        # the call cleared the scratch's status header and no wait ran out
+        assert lib.gdn2_noalloc_status(stream) == 0
