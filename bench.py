@@ -91,11 +91,11 @@ def bytes_per_chunk(C, D, s=4):
         "bwd_intra1": 2 * x + 3 * t + 2 * s2 + 3 * t + cc + 2 * t,   # q k, do vnew kg dvp, h dh; pdq pdk pdgc dAqk dWp dv
         "bwd_intra2": 4 * x + 2 * x + 7 * t + 2 * cc,      # k v w b in, dw dv out; A dAkk, dWp dv gc pdk pdgc in/out pdb
         "bwd_intra3": 4 * x + 2 * cc + 5 * t + 4 * x,      # q k b g; dAqk dAkk; gc pd*; dq dk db dg out
-        "fwd_affine": 3 * t + 2 * s2,
-        "fwd_scan": 3 * s2,
+        "fwd_affine": 3 * t + 3 * s2,                      # kg W U in; M (both ways), Bc out
+        "fwd_scan": 3 * s2,                                # M, Bc in; h out
         "fwd_out": 3 * t + s2 + cc + 3 * t,
         "bwd_prep": cc + 3 * t + t + s2,
-        "bwd_scan": 3 * s2,
+        "bwd_scan": 3 * s2,                                # M^T, E in; dh out
         "bwd_exact": 0,
     }
 

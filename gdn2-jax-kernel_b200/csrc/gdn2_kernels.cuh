@@ -1,6 +1,9 @@
 // Kernel-side declarations and the device building blocks shared by the
 // forward and backward translation units.
 #pragma once
+#ifdef GDN2_PHASE_TIMING
+#include <cstdio>
+#endif
 #include "gdn2_common.cuh"
 #include "gdn2_ws.cuh"
 
@@ -45,38 +48,102 @@ template <int C, int D, int NV> struct StateSmem {
 //         acc = 0;  for k = n .. m-1:  acc = san(acc + T_mk A_kn)
 //         A_mn = san(-A_mm acc)
 // S is transposed (S[j*ld + i] = M(i, j)), holding T below the processed
-// rows and A elsewhere.  `tmp` needs (nb-1) * blk^2 * (C / (blk*nb)) floats.
-__device__ __forceinline__ void wy_compose_seq(float* S, int ld, int C, int blk, int nb, float* tmp,
+// rows and A elsewhere.  `tmp` needs (nb-1) * BLK^2 * (C / (BLK*nb)) floats.
+// Each thread owns a 4 x 4 tile of one output block: a float4 of four
+// consecutive rows of S per contraction step (S is transposed, so rows are
+// contiguous) against four columns, 16 FMAs per 5 shared loads.  ld must keep
+// float4 rows 16-byte aligned (ld % 4 == 0).
+template <int BLK>
+__device__ __forceinline__ void wy_compose_seq(float* S, int ld, int C, int nb, float* tmp,
                                                float clip) {
-  const int per = blk * blk, groups = C / (blk * nb);
+  constexpr int per = BLK * BLK, TPB = (BLK / 4) * (BLK / 4);   // 4 x 4 tiles per block
+  const int groups = C / (BLK * nb);
   for (int m = 1; m < nb; ++m) {
-    const int total = groups * m * per;
-    for (int e = threadIdx.x; e < total; e += kThreads) {   // acc_n of every block (m, n)
-      const int gi = e / (m * per), rem = e % (m * per), n = rem / per, r2 = rem % per;
-      const int i = r2 % blk, j = r2 / blk, o = gi * blk * nb;
-      const int row = o + m * blk + i, col = o + n * blk + j;
-      float acc = 0.f;
+    const int tiles = groups * m * TPB;
+    for (int e = threadIdx.x; e < tiles; e += kThreads) {   // acc_n of every block (m, n)
+      const int gi = e / (m * TPB), rem = e - gi * (m * TPB), n = rem / TPB, tt = rem % TPB;
+      const int ti = tt % (BLK / 4), tj = tt / (BLK / 4), o = gi * BLK * nb;
+      const int row0 = o + m * BLK + 4 * ti, col0 = o + n * BLK + 4 * tj;
+      float acc[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
       for (int k = n; k < m; ++k) {
-        const int x0 = o + k * blk;
-        float sum = 0.f;
-        for (int t = 0; t < blk; ++t) sum = fmaf(S[(x0 + t) * ld + row], S[col * ld + x0 + t], sum);
-        acc = san(acc + sum, clip);
+        float sm4[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sm4[r][c] = 0.f;
+        const int x0 = o + k * BLK;
+#pragma unroll 4
+        for (int t = 0; t < BLK; ++t) {
+          const float4 tv = *reinterpret_cast<const float4*>(S + (x0 + t) * ld + row0);  // T(row0+r, x)
+          float av[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) av[c] = S[(col0 + c) * ld + x0 + t];             // A(x, col0+c)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            sm4[0][c] = fmaf(tv.x, av[c], sm4[0][c]);
+            sm4[1][c] = fmaf(tv.y, av[c], sm4[1][c]);
+            sm4[2][c] = fmaf(tv.z, av[c], sm4[2][c]);
+            sm4[3][c] = fmaf(tv.w, av[c], sm4[3][c]);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[r][c] = san(acc[r][c] + sm4[r][c], clip);
       }
-      tmp[(gi * (nb - 1) + n) * per + j * blk + i] = acc;
+      float* tb = tmp + (gi * (nb - 1) + n) * per;   // tb[j * BLK + i] = acc(i, j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<float4*>(tb + (4 * tj + c) * BLK + 4 * ti) =
+            make_float4(acc[0][c], acc[1][c], acc[2][c], acc[3][c]);
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < total; e += kThreads) {   // A_mn = san(-A_mm acc_n)
-      const int gi = e / (m * per), rem = e % (m * per), n = rem / per, r2 = rem % per;
-      const int i = r2 % blk, j = r2 / blk, o = gi * blk * nb;
-      const int row = o + m * blk + i, col = o + n * blk + j;
-      const float* an = tmp + (gi * (nb - 1) + n) * per + j * blk;
-      const int x0 = o + m * blk;
-      float sum = 0.f;
-      for (int t = 0; t < blk; ++t) sum = fmaf(S[(x0 + t) * ld + row], an[t], sum);
-      S[col * ld + row] = san(-sum, clip);
+    for (int e = threadIdx.x; e < tiles; e += kThreads) {   // A_mn = san(-A_mm acc_n)
+      const int gi = e / (m * TPB), rem = e - gi * (m * TPB), n = rem / TPB, tt = rem % TPB;
+      const int ti = tt % (BLK / 4), tj = tt / (BLK / 4), o = gi * BLK * nb;
+      const int row0 = o + m * BLK + 4 * ti, col0 = o + n * BLK + 4 * tj;
+      const float* tb = tmp + (gi * (nb - 1) + n) * per;
+      const int xm = o + m * BLK;
+      float sm4[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm4[r][c] = 0.f;
+#pragma unroll 4
+      for (int t = 0; t < BLK; ++t) {
+        const float4 av = *reinterpret_cast<const float4*>(S + (xm + t) * ld + row0);   // A_mm(row0+r, t)
+        float bv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) bv[c] = tb[(4 * tj + c) * BLK + t];                // acc(t, col0+c)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          sm4[0][c] = fmaf(av.x, bv[c], sm4[0][c]);
+          sm4[1][c] = fmaf(av.y, bv[c], sm4[1][c]);
+          sm4[2][c] = fmaf(av.z, bv[c], sm4[2][c]);
+          sm4[3][c] = fmaf(av.w, bv[c], sm4[3][c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<float4*>(S + (col0 + c) * ld + row0) =
+            make_float4(san(-sm4[0][c], clip), san(-sm4[1][c], clip), san(-sm4[2][c], clip),
+                        san(-sm4[3][c], clip));
     }
     __syncthreads();
   }
+}
+
+// Sub-block level of the substitution with blocks of bc rows (runtime size,
+// a multiple of 16), dispatched to the unrolled forms.
+__device__ __forceinline__ void wy_compose_blocks(float* S, int ld, int C, int bc, int nb,
+                                                  float* tmp, float clip) {
+  if (bc == 16) wy_compose_seq<16>(S, ld, C, nb, tmp, clip);
+  else if (bc == 32) wy_compose_seq<32>(S, ld, C, nb, tmp, clip);
+  else if (bc == 64) wy_compose_seq<64>(S, ld, C, nb, tmp, clip);
 }
 
 // Row-by-row forward substitution of every 16 x 16 diagonal block
@@ -115,8 +182,8 @@ __device__ __forceinline__ void wy_micro_solves(float* S, int ld, float clip) {
 template <int C>
 __device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, int bc, float clip) {
   wy_micro_solves<C>(S, ld, clip);
-  if (bc > 16) wy_compose_seq(S, ld, C, 16, bc / 16, tmp, clip);
-  if (C > bc) wy_compose_seq(S, ld, C, bc, C / bc, tmp, clip);
+  if (bc > 16) wy_compose_seq<16>(S, ld, C, bc / 16, tmp, clip);
+  if (C > bc) wy_compose_blocks(S, ld, C, bc, C / bc, tmp, clip);
 }
 
 // Column-wise inclusive prefix sum of a C x D tile held row-major in shared
@@ -207,11 +274,22 @@ __device__ __forceinline__ void wy_level_tiled(float* S, int ld, float* tmp, flo
 __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr, int bc,
                                                 float clip) {
   constexpr int C = 128, H = 64, LY = 68;
+#ifdef GDN2_PHASE_TIMING
+  long long t0 = clock64();
+#endif
   wy_micro_solves<C>(S, ld, clip);
+#ifdef GDN2_PHASE_TIMING
+  long long t1 = clock64();
+#endif
   if (bc == 32) wy_level_tiled<16, 2, 2>(S, ld, tmp, clip);            // two 16-row blocks
-  else if (bc > 16) wy_compose_seq(S, ld, C, 16, bc / 16, tmp, clip);   // inside each sub-block
+  else if (bc > 16) wy_compose_seq<16>(S, ld, C, bc / 16, tmp, clip);   // inside each sub-block
+#ifdef GDN2_PHASE_TIMING
+  long long t2 = clock64();
+  if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
+    printf("wy phases: micro %lld level1 %lld\n", t1 - t0, t2 - t1);
+#endif
   if (bc != 64) {
-    if (C > bc) wy_compose_seq(S, ld, C, bc, C / bc, tmp, clip);
+    if (C > bc) wy_compose_blocks(S, ld, C, bc, C / bc, tmp, clip);
     return;
   }
   // last level: T10 = M(64.., 0..63), A00 = A(0..63, 0..63), A11 = A(64.., 64..)

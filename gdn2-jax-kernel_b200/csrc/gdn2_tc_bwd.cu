@@ -6,6 +6,27 @@
 #include "gdn2_kernels.cuh"
 #include "gdn2_tc_stage.cuh"
 
+// Optional per-phase cycle counts of one CTA (build with -DGDN2_PHASE_TIMING;
+// the counts are printed by that CTA).  Compiled out otherwise.
+#ifdef GDN2_PHASE_TIMING
+#include <cstdio>
+#define GDN2_TMARK(i) \
+  do { if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) tmark[i] = clock64(); } while (0)
+#define GDN2_TPRINT(name, n)                                                         \
+  do {                                                                               \
+    if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) {                           \
+      printf("%s phases:", name);                                                    \
+      for (int i_ = 1; i_ < n; ++i_) printf(" %lld", tmark[i_] - tmark[i_ - 1]);     \
+      printf("\n");                                                                 \
+    }                                                                                \
+  } while (0)
+#define GDN2_TDECL long long tmark[16]
+#else
+#define GDN2_TMARK(i) do { } while (0)
+#define GDN2_TPRINT(name, n) do { } while (0)
+#define GDN2_TDECL
+#endif
+
 namespace gdn2 {
 
 using namespace tc;
@@ -457,6 +478,8 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const float* dAkkT = ws.dAkkT + chunk * C * C;
   float* red = &ts.colpart[0][0];
   float* sdg = sm;   // [C][D] after the products (ring area)
+  GDN2_TDECL;
+  GDN2_TMARK(0);
 
   const uint32_t tmem = setup(&ts);
   // gc tile resident in shared memory after the ring: read by every operand
@@ -490,6 +513,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread || p.bc < 32;
   const int JW = (block_max(spread64, red) <= 80.f && p.bc % 64 == 0) ? 64 : 32;
   bool run_exact = exact;
+  GDN2_TMARK(1);
 
   if (!exact) {
     Ring ring = ring_of(sm, &ts, 2);
@@ -511,6 +535,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     float gg0 = 0.f, gg1 = 0.f, gg2 = 0.f, gg3 = 0.f;   // dgc terms of each pass
 #pragma unroll 1
     for (int pass = 0; pass < 4; ++pass) {
+      if (pass > 0) GDN2_TMARK(1 + 2 * pass);
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
       const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
       for (int sl = 0; sl < 4; ++sl, ++gs) {
@@ -550,6 +575,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         }
       }
       drain(&ts.done, ph, ws.status);
+      GDN2_TMARK(2 + 2 * pass);
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
         const int c0 = cb + qd * 16;
@@ -668,6 +694,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       }
     }
     const float lim = p.clip * (1.f - 1e-5f);   // NaN fails every test below
+    GDN2_TMARK(9);
     const bool bad = !(gq_dq < lim && gq_dbk < lim && gq_dk2 + gq_dk3 < lim &&
                        gg0 + gg1 + gg2 + gg3 < lim);
     run_exact = __syncthreads_or(bad);
@@ -693,6 +720,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, GLD, dAqkT, dAkkT, pdq, pdk, pdb, pdgc, dq_out,
                       dk_out, db_out, off, sdg, p.scale, p.clip);
   }
+  GDN2_TMARK(10);
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);
   for_tile([&](int i, int d) {
@@ -701,6 +729,8 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
            san4(san4(v4, p.clip), kFinalClipTc));
   });
   teardown(tmem);
+  GDN2_TMARK(11);
+  GDN2_TPRINT("bwd_intra3", 12);
 }
 
 template <typename T>
