@@ -31,11 +31,12 @@ __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
                                const float* gc, int gld, const float* __restrict__ dAqkT,
                                const float* __restrict__ dAkkT, const float* pdq, const float* pdk,
                                const float* pdb, const float* pdgc, T* dq_out, T* dk_out,
-                               T* db_out, long off, float* sdg, float scale, float clip) {
+                               T* db_out, long off, float* sdg, float scale, float clip,
+                               int gates) {
   const int nsub = C / BC;
   for (int e = threadIdx.x; e < C * D; e += kThreads) {
     const int x = e / D, d = e % D, X = x / BC;
-    const float kx = to_f<T>(kc[x * rs + d]), bx = to_f<T>(bc[x * rs + d]);
+    const float kx = to_f<T>(kc[x * rs + d]), bx = ld_gate<T>(bc + x * rs + d, gates, kGateB);
     const float lqx = scale * to_f<T>(qc[x * rs + d]), lkx = bx * kx;
     const float gx = gc[x * gld + d];
     float dq = 0.f, dbk = 0.f, dk = 0.f, dgc = 0.f;
@@ -66,7 +67,7 @@ __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
             const float cm = (dd >= -20.f && dd <= 20.f) ? 1.f : 0.f;
             const float mq = dAqkT[x * C + y], mk = dAkkT[x * C + y];
             const float lqy = scale * to_f<T>(qc[y * rs + d]) * ed;
-            const float lky = to_f<T>(bc[y * rs + d]) * to_f<T>(kc[y * rs + d]) * ed;
+            const float lky = ld_gate<T>(bc + y * rs + d, gates, kGateB) * to_f<T>(kc[y * rs + d]) * ed;
             drq = fmaf(mq, lqy, drq);
             drk = fmaf(mk, lky, drk);
             wqj = fmaf(mq * lqy, kx * cm, wqj);
@@ -88,7 +89,8 @@ __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
     const long o = off + x * rs + d;
     dq_out[o] = from_f<T>(san(pdq[e] + san(dq, clip), kB4FinalClip));
     dk_out[o] = from_f<T>(san(pdk[e] + san(dk + dbk * bx, clip), kB4FinalClip));
-    db_out[o] = from_f<T>(san(pdb[e] + san(dbk * kx, clip), kB4FinalClip));
+    const float dbo = san(pdb[e] + san(dbk * kx, clip), kB4FinalClip);
+    db_out[o] = from_f<T>(gates ? dbo * bx * (1.f - bx) : dbo);
     sdg[e] = pdgc[e] + san(dgc, clip);
   }
 }

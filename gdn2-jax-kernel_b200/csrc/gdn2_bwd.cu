@@ -234,7 +234,7 @@ k_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* __re
 //   dA = san(dWp kb^T + dv wv^T); tmp = san(dA A^T); dAkk = -(A^T tmp) * strict
 //   dkb = A^T dWp; dwv = A^T dv  ->  dk, db, dgc partials; dw, dv final.
 // ---------------------------------------------------------------------------
-template <typename T, int C, int D>
+template <typename T, int C, int D, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ w,
              const T* __restrict__ b, T* __restrict__ dv_out, T* __restrict__ dw_out, Problem p,
@@ -256,7 +256,7 @@ k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restri
   load_tile_T<float>(X1, LDC, ws.dWp + chunk * C * D, D, C, D);     // X1[d][i] = dWp(i,d)
   for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
     const int j = e % C, d = (e / C) * 4;
-    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
     const float* g4 = gc + j * D + d;
     X2[(d + 0) * LDC + j] = bv.x * kv.x * __expf(g4[0]);
     X2[(d + 1) * LDC + j] = bv.y * kv.y * __expf(g4[1]);
@@ -271,7 +271,7 @@ k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restri
   load_tile_T<float>(X1, LDC, ws.dv + chunk * C * D, D, C, D);      // X1[d][i] = dv(i,d)
   for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
     const int j = e % C, d = (e / C) * 4;
-    const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
+    const float4 wv = ld4_gate<T>(wc + j * rs + d, GATES, kGateW), vv = ld4<T>(vc + j * rs + d);
     X2[(d + 0) * LDC + j] = wv.x * vv.x;
     X2[(d + 1) * LDC + j] = wv.y * vv.y;
     X2[(d + 2) * LDC + j] = wv.z * vv.z;
@@ -337,7 +337,7 @@ k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restri
       for (int jj = 0; jj < TD::TN_; ++jj) {
         const int d = t.c0 + jj;
         const float eg = __expf(gc[j * D + d]);
-        const float kk = to_f<T>(kc[j * rs + d]), bv = to_f<T>(bc[j * rs + d]);
+        const float kk = to_f<T>(kc[j * rs + d]), bv = ld_gate<T>(bc + j * rs + d, GATES, kGateB);
         const float dkb = t.acc[ii][jj];
         ok[jj] = san(pdk[j * D + d] + dkb * eg * bv, p.clip);
         ob[jj] = san(dkb * eg * kk, p.clip);
@@ -362,10 +362,10 @@ k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restri
       for (int jj = 0; jj < TD::TN_; ++jj) {
         const int d = t.c0 + jj;
         const float dwv = t.acc[ii][jj];
-        dw_out[off + j * rs + d] =
-            from_f<T>(san(san(dwv * to_f<T>(vc[j * rs + d]), p.clip), kFinalClip));
-        dv_out[off + j * rs + d] =
-            from_f<T>(san(san(dwv * to_f<T>(wc[j * rs + d]), p.clip), kFinalClip));
+        const float wa = ld_gate<T>(wc + j * rs + d, GATES, kGateW);
+        const float dwo = san(san(dwv * to_f<T>(vc[j * rs + d]), p.clip), kFinalClip);
+        dw_out[off + j * rs + d] = from_f<T>(GATES ? dwo * wa * (1.f - wa) : dwo);
+        dv_out[off + j * rs + d] = from_f<T>(san(san(dwv * wa, p.clip), kFinalClip));
       }
     }
   }
@@ -380,7 +380,7 @@ k_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restri
 // pair sum of the weights.  Chunks with any g > 0 use the exact elementwise
 // form with the +-20 clip and its mask.
 // ---------------------------------------------------------------------------
-template <typename T, int C, int D>
+template <typename T, int C, int D, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ b,
              const T* __restrict__ g, T* __restrict__ dq_out, T* __restrict__ dk_out,
@@ -410,7 +410,7 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
 
   float gpos = -1.f;
   for (int e = threadIdx.x; e < C * D; e += kThreads)
-    gpos = fmaxf(gpos, to_f<T>(gcp[(e / D) * rs + e % D]));
+    gpos = fmaxf(gpos, ld_gate<T>(gcp + (e / D) * rs + e % D, GATES, kGateG));
   // positive gates, or sub-blocks that do not hold whole row groups (the
   // clip guard below needs partials per BC block), take the exact path
   const bool exact = block_max(gpos, red) > 0.f || p.bc % GS != 0;
@@ -495,13 +495,13 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
         const int d = t.c0 + jj;
         const float f = __expf(gc[i * D + d] - gc[t.r0 * D + d]);
         const float dbk = t.acc[ii][jj] * f;
-        const float kk = to_f<T>(kc[i * rs + d]), bv = to_f<T>(bc[i * rs + d]);
+        const float kk = to_f<T>(kc[i * rs + d]), bv = ld_gate<T>(bc + i * rs + d, GATES, kGateB);
         gd_dbk = fmaxf(gd_dbk, sab[ii][jj] * f);
         gg1 = fmaxf(gg1, fabsf(bv * kk) * sab[ii][jj] * f);
         dka[ii][jj] = dbk * bv;
         sdg[i * D + d] += bv * kk * dbk;
-        db_out[off + i * rs + d] =
-            from_f<T>(san(pdb[i * D + d] + san(dbk * kk, p.clip), kFinalClip));
+        const float dbo = san(pdb[i * D + d] + san(dbk * kk, p.clip), kFinalClip);
+        db_out[off + i * rs + d] = from_f<T>(GATES ? dbo * bv * (1.f - bv) : dbo);
       }
     }
     __syncthreads();
@@ -537,7 +537,7 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
     load_tile_T<float>(X1, LDC, dAkkT, C, C, C);
     for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
       const int i = e / (D / 4), d = (e % (D / 4)) * 4;
-      const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4<T>(bc + i * rs + d);
+      const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4_gate<T>(bc + i * rs + d, GATES, kGateB);
       const float* gi = gc + i * D + d;
       const float* gr = gc + (i & ~(GS - 1)) * D + d;
       *reinterpret_cast<float4*>(X2 + i * LDD + d) = make_float4(
@@ -570,13 +570,15 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
   if (run_exact) {
     // the reference's pair order (overwrites the fast path's outputs)
     b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, D, dAqkT, dAkkT, pdq, pdk, pdb, pdgc,
-                      dq_out, dk_out, db_out, off, sdg, p.scale, p.clip);
+                      dq_out, dk_out, db_out, off, sdg, p.scale, p.clip, GATES);
   }
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);
   for (int e = threadIdx.x; e < C * D; e += kThreads) {
     const int i = e / D, d = e % D;
-    dg_out[off + i * rs + d] = from_f<T>(san(san(sdg[e], p.clip), kFinalClip));
+    float dgo = san(san(sdg[e], p.clip), kFinalClip);
+    if (GATES) dgo *= -gate_sig(to_f<T>(gcp[i * rs + d]));   // d(-softplus(g'))/dg'
+    dg_out[off + i * rs + d] = from_f<T>(dgo);
   }
 }
 
@@ -616,7 +618,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
   if (!skip12) {
     hook.begin(kStageBwdIntra2, s);
     const size_t smem = (size_t)(2 * BIG) * sizeof(float);
-    auto kern = k_bwd_intra2<T, C, D>;
+    auto kern = p.gates ? k_bwd_intra2<T, C, D, true> : k_bwd_intra2<T, C, D, false>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, s>>>(k, v, w, b, dv, dw, p, ws);
@@ -628,7 +630,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
     using TD = typename TileFor<C, D>::type;
     constexpr int NG = C / TD::TM_;
     const size_t smem = (size_t)(2 * BIG + C * D + NG * D + 256) * sizeof(float);
-    auto kern = k_bwd_intra3<T, C, D>;
+    auto kern = p.gates ? k_bwd_intra3<T, C, D, true> : k_bwd_intra3<T, C, D, false>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, s>>>(q, k, b, g, dq, dk, db, dg, p, ws);

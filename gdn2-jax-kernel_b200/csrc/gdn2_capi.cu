@@ -26,6 +26,7 @@ struct Profiler {
 };
 Profiler g_prof;
 std::mutex g_prof_mu;
+int g_diag = 0;   // per-stage diagnostics on (gdn2_diag_enable)
 
 void prof_hook(int stage, int end, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -60,6 +61,7 @@ int cuda_fail(cudaError_t e, const char* where) {
 }
 
 int validate(int dtype, int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
+  dtype &= ~GDN2_GATES_RAW;
   if (dtype != GDN2_F32 && dtype != GDN2_BF16)
     return fail(GDN2_ERR_INVALID, "unsupported dtype code %s%ld", "", dtype);
   if (B <= 0 || T <= 0 || H <= 0)
@@ -169,6 +171,8 @@ int clear_status(const Workspace& ws, cudaStream_t s) {
 Problem make_problem(int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
   Problem p;
   p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT; p.bc = BC;
+  p.diag = g_diag;
+  p.gates = 0;
   p.scale = scale; p.clip = clip;
   return p;
 }
@@ -192,6 +196,32 @@ size_t gdn2_status_offset(const void* workspace) {
 }
 
 extern "C" {
+
+int gdn2_diag_enable(int on) {
+  g_diag = on != 0;
+  return GDN2_OK;
+}
+
+int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
+                   int* nonfinite, float* maxabs) {
+  if (!workspace || workspace_bytes < 512 || n < 0 || n > kNumDiag)
+    return fail(GDN2_ERR_INVALID, "%sgdn2_diag_read: bad workspace or stage count");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int* hdr = reinterpret_cast<const int*>(static_cast<const char*>(workspace) +
+                                                gdn2_status_offset(workspace));
+  int host[2 * kNumDiag];
+  cudaError_t e = cudaMemcpyAsync(host, hdr + kDiagBase, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_diag_read");
+  for (int i = 0; i < n; ++i) {
+    if (nonfinite) nonfinite[i] = host[2 * i];
+    if (maxabs) {
+      int bits = host[2 * i + 1];
+      memcpy(&maxabs[i], &bits, sizeof(float));
+    }
+  }
+  return kNumDiag;
+}
 
 int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace || workspace_bytes < 512)
@@ -256,7 +286,9 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  p.gates = (dtype & GDN2_GATES_RAW) != 0;
+  dtype &= ~GDN2_GATES_RAW;
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, false);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;
@@ -285,7 +317,9 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  p.gates = (dtype & GDN2_GATES_RAW) != 0;
+  dtype &= ~GDN2_GATES_RAW;
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, true);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;

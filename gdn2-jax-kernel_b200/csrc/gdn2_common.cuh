@@ -225,4 +225,70 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
+// Gate activations fused into the loads (GDN2_GATES_RAW): the caller passes
+// the pre-activations, and the kernels read w = sigmoid(w'), b = sigmoid(b'),
+// g = -softplus(g') (the activations the reference leaves to its caller,
+// README.md:60-68).  Gradients leave with the chain rule applied:
+// dw' = dw w (1 - w), db' = db b (1 - b), dg' = -dg sigmoid(g').
+enum Gate { kGateW = 0, kGateB, kGateG };
+__device__ __forceinline__ float gate_sig(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float gate_act(float x, int gate) {
+  return gate == kGateG ? -(fmaxf(x, 0.f) + log1pf(expf(-fabsf(x)))) : gate_sig(x);
+}
+__device__ __forceinline__ float4 gate_act4(float4 v, int gate) {
+  return make_float4(gate_act(v.x, gate), gate_act(v.y, gate), gate_act(v.z, gate),
+                     gate_act(v.w, gate));
+}
+template <typename T>
+__device__ __forceinline__ float4 ld4_gate(const T* p, int raw, int gate) {
+  const float4 v = ld4<T>(p);
+  return raw ? gate_act4(v, gate) : v;
+}
+template <typename T>
+__device__ __forceinline__ float ld_gate(const T* p, int raw, int gate) {
+  const float x = to_f<T>(*p);
+  return raw ? gate_act(x, gate) : x;
+}
+// d(sigmoid)/dx from the activated value s
+__device__ __forceinline__ float4 sig_grad4(float4 s) {
+  return make_float4(s.x * (1.f - s.x), s.y * (1.f - s.y), s.z * (1.f - s.z), s.w * (1.f - s.w));
+}
+__device__ __forceinline__ float4 mul4(float4 a, float4 b) {
+  return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+
+// Per-stage diagnostics (the reference's _stage_diag, gdn2_fwd.py:47-76):
+// non-finite count and largest finite |x| of a stage output, accumulated per
+// thread and merged per warp into the workspace status header (ints
+// kDiagBase + 2 s, kDiagBase + 2 s + 1 for stage s; the header is cleared by
+// every call).  Only used when Problem::diag is set.
+enum DiagStage {
+  kDiagAqk = 0, kDiagAkk, kDiagA, kDiagW, kDiagU, kDiagKg, kDiagQg, kDiagO, kDiagHFinal,
+  kNumDiag
+};
+constexpr int kDiagBase = 16;   // ints: byte offset 64 of the status header
+struct StageDiag {
+  float mx = 0.f;
+  int nf = 0;
+  __device__ __forceinline__ void add(float x) {
+    if (isfinite(x)) mx = fmaxf(mx, fabsf(x));
+    else ++nf;
+  }
+  __device__ __forceinline__ void add4(float4 v) { add(v.x); add(v.y); add(v.z); add(v.w); }
+  // every lane of the warp calls this
+  __device__ __forceinline__ void flush(int* hdr, int stage) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      nf += __shfl_xor_sync(0xffffffffu, nf, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      if (nf) atomicAdd(hdr + kDiagBase + 2 * stage, nf);
+      atomicMax(hdr + kDiagBase + 2 * stage + 1, __float_as_int(mx));   // mx >= 0
+    }
+    mx = 0.f;
+    nf = 0;
+  }
+};
+
 }  // namespace gdn2

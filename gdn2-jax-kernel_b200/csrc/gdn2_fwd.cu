@@ -16,7 +16,7 @@ namespace gdn2 {
 // -20 changes values by < e^-20.  Chunks with any g > 0 take the exact
 // elementwise path with the reference's +-20 clip.
 // ---------------------------------------------------------------------------
-template <typename T, int C, int D>
+template <typename T, int C, int D, bool DIAG, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
             const T* __restrict__ w, const T* __restrict__ b, const T* __restrict__ g,
@@ -41,6 +41,9 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
   // ---- gc = in-chunk cumsum of g (gdn2_fwd.py:105-107)
   load_tile<T>(sgc, D, gcp, rs, C, D);
   __syncthreads();
+  if (GATES)   // g = -softplus(g') fused into the load
+    for (int e = threadIdx.x; e < C * D; e += kThreads) sgc[e] = gate_act(sgc[e], kGateG);
+  __syncthreads();
   float gpos = -1.f;
   for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[e]);
   const bool exact = block_max(gpos, red) > 0.f;
@@ -54,6 +57,7 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
   }
 
   float* aqkT = ws.AqkT + chunk * C * C;
+  StageDiag dga, dgb;   // stage diagnostics (p.diag only)
   if (!exact) {
     // ---- Kernel A, factored: R^T into Y, L^T into X (contraction index d outer)
     for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
@@ -84,6 +88,7 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
       for (int ii = 0; ii < TC::TM_; ++ii) {
         const int i = t.r0 + ii;
         o4[ii] = (j <= i) ? san(p.scale * t.acc[ii][jj], p.clip) : 0.f;
+        if (DIAG) dga.add(o4[ii]);
       }
       store_vec<TC::TM_>(aqkT + j * C + t.r0, o4);
     }
@@ -92,7 +97,7 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
     for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
       const int j = e % C, d = (e / C) * 4;
       const float4 kv = ld4<T>(kc + j * rs + d);
-      const float4 bv = ld4<T>(bc + j * rs + d);
+      const float4 bv = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
       const int jr = j & ~(GS - 1);
       const float* gj = sgc + j * D + d;
       const float* gr = sgc + jr * D + d;
@@ -114,6 +119,7 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
       for (int ii = 0; ii < TC::TM_; ++ii) {
         const int i = t.r0 + ii;
         o4[ii] = (j < i) ? san(t.acc[ii][jj], p.clip) : 0.f;
+        if (DIAG) dgb.add(o4[ii]);
       }
       store_vec<TC::TM_>(X + j * LDC + t.r0, o4);
     }
@@ -127,12 +133,20 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
           const float ed = __expf(fminf(fmaxf(sgc[i * D + d] - sgc[j * D + d], -20.f), 20.f));
           const float kj = to_f<T>(kc[j * rs + d]) * ed;
           sq = fmaf(to_f<T>(qc[i * rs + d]), kj, sq);
-          sk = fmaf(to_f<T>(bc[i * rs + d]) * to_f<T>(kc[i * rs + d]), kj, sk);
+          sk = fmaf(ld_gate<T>(bc + i * rs + d, GATES, kGateB) * to_f<T>(kc[i * rs + d]), kj, sk);
         }
       }
       aqkT[j * C + i] = (j <= i) ? san(p.scale * sq, p.clip) : 0.f;
       X[j * LDC + i] = (j < i) ? san(sk, p.clip) : 0.f;
+      if (DIAG) {
+        dga.add(aqkT[j * C + i]);
+        dgb.add(X[j * LDC + i]);
+      }
     }
+  }
+  if (DIAG) {
+    dga.flush(ws.status, kDiagAqk);
+    dgb.flush(ws.status, kDiagAkk);
   }
   __syncthreads();
 
@@ -142,14 +156,17 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
     float* at = ws.AT + chunk * C * C;
     for (int e = threadIdx.x * 4; e < C * C; e += kThreads * 4) {
       const int r = e / C, cc = e % C;
-      *reinterpret_cast<float4*>(at + e) = *reinterpret_cast<const float4*>(X + r * LDC + cc);
+      const float4 a4 = *reinterpret_cast<const float4*>(X + r * LDC + cc);
+      *reinterpret_cast<float4*>(at + e) = a4;
+      if (DIAG) dga.add4(a4);
     }
+    if (DIAG) dga.flush(ws.status, kDiagA);
   }
 
   // ---- Kernel C: W = A (b k e^gc), U = A (w v)
   for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
     const int j = e / (D / 4), d = (e % (D / 4)) * 4;
-    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
     const float* gj = sgc + j * D + d;
     float4 o = make_float4(bv.x * kv.x * __expf(gj[0]), bv.y * kv.y * __expf(gj[1]),
                            bv.z * kv.z * __expf(gj[2]), bv.w * kv.w * __expf(gj[3]));
@@ -165,13 +182,17 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
     for (int jj = 0; jj < TD::TN_; ++jj) {
       float o4[TD::TM_];
 #pragma unroll
-      for (int ii = 0; ii < TD::TM_; ++ii) o4[ii] = san(t.acc[ii][jj], p.clip);
+      for (int ii = 0; ii < TD::TM_; ++ii) {
+        o4[ii] = san(t.acc[ii][jj], p.clip);
+        if (DIAG) dga.add(o4[ii]);
+      }
       store_vec<TD::TM_>(wt + (t.c0 + jj) * C + t.r0, o4);
     }
+    if (DIAG) dga.flush(ws.status, kDiagW);
     __syncthreads();
     for (int e = threadIdx.x; e < C * (D / 4); e += kThreads) {
       const int j = e / (D / 4), d = (e % (D / 4)) * 4;
-      const float4 wv = ld4<T>(wc + j * rs + d), vv = ld4<T>(vc + j * rs + d);
+      const float4 wv = ld4_gate<T>(wc + j * rs + d, GATES, kGateW), vv = ld4<T>(vc + j * rs + d);
       *reinterpret_cast<float4*>(Y + j * LDD + d) =
           make_float4(wv.x * vv.x, wv.y * vv.y, wv.z * vv.z, wv.w * vv.w);
     }
@@ -183,9 +204,13 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
     for (int ii = 0; ii < TD::TM_; ++ii) {
       float o4[TD::TN_];
 #pragma unroll
-      for (int jj = 0; jj < TD::TN_; ++jj) o4[jj] = san(t.acc[ii][jj], p.clip);
+      for (int jj = 0; jj < TD::TN_; ++jj) {
+        o4[jj] = san(t.acc[ii][jj], p.clip);
+        if (DIAG) dga.add(o4[jj]);
+      }
       store_vec<TD::TN_>(u + (t.r0 + ii) * D + t.c0, o4);
     }
+    if (DIAG) dga.flush(ws.status, kDiagU);
   }
   // kg = k e^{gc_last - gc} (row-major), qg = q e^{gc} (transposed)
   {
@@ -201,11 +226,15 @@ k_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restric
                              san(kv.z * __expf(gl[d + 2] - gi[2]), p.clip),
                              san(kv.w * __expf(gl[d + 3] - gi[3]), p.clip));
       *reinterpret_cast<float4*>(kgo + i * D + d) = o;
+      if (DIAG) dga.add4(o);
     }
+    if (DIAG) dga.flush(ws.status, kDiagKg);
     for (int e = threadIdx.x; e < C * D; e += kThreads) {
       const int i = e % C, d = e / C;
       qgo[d * C + i] = san(to_f<T>(qc[i * rs + d]) * __expf(sgc[i * D + d]), p.clip);
+      if (DIAG) dga.add(qgo[d * C + i]);
     }
+    if (DIAG) dga.flush(ws.status, kDiagQg);
   }
 }
 
@@ -237,6 +266,7 @@ k_fwd_state(Problem p, Workspace ws, const float* __restrict__ h0, float* __rest
     sh[e] = h0 ? san(h0[bh * D * D + d * D + v0 + vv], p.clip) : 0.f;
   }
   __syncthreads();
+  StageDiag dgo;   // o, then h_final (p.diag only)
   for (int c = 0; c < p.nc; ++c) {
     const size_t chunk = bh * p.nc + c;
     if (save) {
@@ -283,7 +313,10 @@ k_fwd_state(Problem p, Workspace ws, const float* __restrict__ h0, float* __rest
       for (int ii = 0; ii < T1::TM_; ++ii) {
         float o4[T1::TN_];
 #pragma unroll
-        for (int jj = 0; jj < T1::TN_; ++jj) o4[jj] = san(t.acc[ii][jj], p.clip);
+        for (int jj = 0; jj < T1::TN_; ++jj) {
+          o4[jj] = san(t.acc[ii][jj], p.clip);
+          if (p.diag) dgo.add(o4[jj]);
+        }
         store_vec<T1::TN_>(orow + (t.r0 + ii) * rs + t.c0, o4);
       }
     }
@@ -309,9 +342,14 @@ k_fwd_state(Problem p, Workspace ws, const float* __restrict__ h0, float* __rest
     }
     __syncthreads();
   }
-  if (hfinal)
-    for (int e = threadIdx.x; e < D * NV; e += kThreads)
+  if (p.diag && o) dgo.flush(ws.status, kDiagO);
+  if (hfinal) {
+    for (int e = threadIdx.x; e < D * NV; e += kThreads) {
       hfinal[bh * D * D + (e / NV) * D + v0 + e % NV] = sh[e];
+      if (p.diag) dgo.add(sh[e]);
+    }
+    if (p.diag) dgo.flush(ws.status, kDiagHFinal);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -320,7 +358,8 @@ cudaError_t launch_fwd_intra(const T* q, const T* k, const T* v, const T* w, con
                              const T* g, const Problem& p, const Workspace& ws,
                              cudaStream_t s) {
   const size_t smem = FwdSmem<C, D>::bytes();
-  auto kern = k_fwd_intra<T, C, D>;
+  auto kern = p.diag ? (p.gates ? k_fwd_intra<T, C, D, true, true> : k_fwd_intra<T, C, D, true, false>)
+                     : (p.gates ? k_fwd_intra<T, C, D, false, true> : k_fwd_intra<T, C, D, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<dim3(p.nc, p.H, p.B), kThreads, smem, s>>>(q, k, v, w, b, g, p, ws);

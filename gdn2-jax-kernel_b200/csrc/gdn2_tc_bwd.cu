@@ -251,7 +251,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
 // TMEM into resident shared-memory B tiles, and tmp is formed transposed so
 // that its accumulator is already the TMEM A operand of dAkk^T.
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ w,
                 const T* __restrict__ b, T* __restrict__ dv_out, T* __restrict__ dw_out, Problem p,
@@ -295,7 +295,7 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   for_tile([&](int j, int d) {
     const float4 x = lds4(t0 + j * TLD + d);
     const float4 eg = exp4(ldg4(gc + j * D + d));
-    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4<T>(bc + j * rs + d);
+    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
     const float4 pk = ldg4(pdk + j * D + d), pg = ldg4(pdgc + j * D + d);
     st4(pdk + j * D + d, san(pk.x + x.x * eg.x * bv.x, p.clip), san(pk.y + x.y * eg.y * bv.y, p.clip),
         san(pk.z + x.z * eg.z * bv.z, p.clip), san(pk.w + x.w * eg.w * bv.w, p.clip));
@@ -306,10 +306,11 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
         san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
     // dwv -> dw, dv (same pass: more independent loads in flight)
     const float4 y = lds4(t1 + j * TLD + d);
-    const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4<T>(wc + j * rs + d);
+    const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4_gate<T>(wc + j * rs + d, GATES, kGateW);
     const float4 dw = make_float4(y.x * vv.x, y.y * vv.y, y.z * vv.z, y.w * vv.w);
     const float4 dvv = make_float4(y.x * wv.x, y.y * wv.y, y.z * wv.z, y.w * wv.w);
-    st4<T>(dw_out + off + j * rs + d, san4(san4(dw, p.clip), kFinalClipTc));
+    const float4 dwo = san4(san4(dw, p.clip), kFinalClipTc);
+    st4<T>(dw_out + off + j * rs + d, GATES ? mul4(dwo, sig_grad4(wv)) : dwo);
     st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
   });
   fence_before_sync();
@@ -335,7 +336,7 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
         rc(it, j, cc);
         const int d = sl * KS + cc;
         fx.v[it] = ld4<T>(kc + j * rs + d);
-        fy.v[it] = ld4<T>(bc + j * rs + d);
+        fy.v[it] = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
         fz.v[it] = ldg4(gc + j * D + d);
       }
     };
@@ -345,7 +346,7 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
         int j, cc;
         rc(it, j, cc);
         const int d = sl * KS + cc;
-        fx.v[it] = ld4<T>(wc + j * rs + d);
+        fx.v[it] = ld4_gate<T>(wc + j * rs + d, GATES, kGateW);
         fy.v[it] = ld4<T>(vc + j * rs + d);
       }
     };
@@ -455,7 +456,7 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
 // is dgc_i += L_i dL_i, dgc_j -= k_j dR_j.  The dk and dgc partials stay in
 // registers (thread = TMEM row) across the passes.
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ b,
                 const T* __restrict__ g, T* __restrict__ dq_out, T* __restrict__ dk_out,
@@ -497,7 +498,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll 8
   for (int it = 0; it < C * D / 4 / kThreads; ++it) {
     const int e = threadIdx.x + it * kThreads;
-    const float4 g4 = ld4<T>(gcp + (e >> 5) * rs + (e & 31) * 4);
+    const float4 g4 = ld4_gate<T>(gcp + (e >> 5) * rs + (e & 31) * 4, GATES, kGateG);
     gpos = fmaxf(gpos, fmaxf(fmaxf(g4.x, g4.y), fmaxf(g4.z, g4.w)));
   }
   const float gmax = block_max(gpos, red);
@@ -561,7 +562,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
               const float4 qv = ld4<T>(qc + i * rs + d);
               lv = make_float4(p.scale * qv.x, p.scale * qv.y, p.scale * qv.z, p.scale * qv.w);
             } else {
-              const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4<T>(bc + i * rs + d);
+              const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4_gate<T>(bc + i * rs + d, GATES, kGateB);
               lv = make_float4(bv.x * kv.x, bv.y * kv.y, bv.z * kv.z, bv.w * kv.w);
             }
             return make_float4(lv.x * __expf(gi.x - gr.x), lv.y * __expf(gi.y - gr.y),
@@ -633,7 +634,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll
           for (int t = 0; t < 16; t += 4) {
             xa[t / 4] = ld4<T>(kc + x * rs + c0 + t);
-            xb[t / 4] = ld4<T>(bc + x * rs + c0 + t);
+            xb[t / 4] = ld4_gate<T>(bc + x * rs + c0 + t, GATES, kGateB);
           }
           float4 pbv[4];
 #pragma unroll
@@ -649,6 +650,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             for (int u = 0; u < 4; ++u) {
               const float dbk = val[t + u];
               o[u] = san(pv[u] + san(dbk * kv[u], p.clip), kFinalClipTc);
+              if (GATES) o[u] *= bv[u] * (1.f - bv[u]);
               dkr[qd * 16 + t + u] = dbk * bv[u];
               dgr[qd * 16 + t + u] += bv[u] * kv[u] * dbk;
               gq_dbk = fmaxf(gq_dbk, sab[t + u]);
@@ -718,15 +720,20 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     // the reference's pair order: positive gates, wide gate spreads, BC < 32,
     // or a chunk whose guard failed (its fast-path outputs are overwritten)
     b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, GLD, dAqkT, dAkkT, pdq, pdk, pdb, pdgc, dq_out,
-                      dk_out, db_out, off, sdg, p.scale, p.clip);
+                      dk_out, db_out, off, sdg, p.scale, p.clip, GATES);
   }
   GDN2_TMARK(10);
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);
   for_tile([&](int i, int d) {
     const float4 v4 = ldg4(sdg + i * D + d);
-    st4<T>(dg_out + off + i * rs + d,
-           san4(san4(v4, p.clip), kFinalClipTc));
+    float4 dgo = san4(san4(v4, p.clip), kFinalClipTc);
+    if (GATES) {   // d(-softplus(g'))/dg' = -sigmoid(g')
+      const float4 gr = ld4<T>(gcp + i * rs + d);
+      dgo = make_float4(-dgo.x * gate_sig(gr.x), -dgo.y * gate_sig(gr.y), -dgo.z * gate_sig(gr.z),
+                        -dgo.w * gate_sig(gr.w));
+    }
+    st4<T>(dg_out + off + i * rs + d, dgo);
   });
   teardown(tmem);
   GDN2_TMARK(11);
@@ -739,12 +746,11 @@ cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g,
                                  cudaStream_t s, const LaunchHook& hook) {
   // ring (also the C x D dgc tile at the end), then the gc tile
   constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES + (size_t)C * (D + 4) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(k_tc_bwd_intra3<T>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kern = p.gates ? k_tc_bwd_intra3<T, true> : k_tc_bwd_intra3<T, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   hook.begin(kStageBwdIntra3, s);
-  k_tc_bwd_intra3<T><<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, b, g, dq, dk, db, dg,
-                                                                          p, ws);
+  kern<<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, b, g, dq, dk, db, dg, p, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdIntra3, s);
   return cudaSuccess;
@@ -771,15 +777,16 @@ cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w
   if ((e = cudaFuncSetAttribute(k_tc_bwd_intra1<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)smem)) != cudaSuccess)
     return e;
-  if ((e = cudaFuncSetAttribute(k_tc_bwd_intra2<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem)) != cudaSuccess)
+  auto kern2 = p.gates ? k_tc_bwd_intra2<T, true> : k_tc_bwd_intra2<T, false>;
+  if ((e = cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+      cudaSuccess)
     return e;
   hook.begin(kStageBwdIntra1, s);
   k_tc_bwd_intra1<T><<<nchunks, kThreads, smem, s>>>(q, k, dout, dh_final, p, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdIntra1, s);
   hook.begin(kStageBwdIntra2, s);
-  k_tc_bwd_intra2<T><<<nchunks, kThreads, smem, s>>>(k, v, w, b, dv_out, dw_out, p, ws);
+  kern2<<<nchunks, kThreads, smem, s>>>(k, v, w, b, dv_out, dw_out, p, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdIntra2, s);
   return cudaSuccess;

@@ -52,7 +52,7 @@ __device__ __forceinline__ void sts4(float* p, float4 v) { *reinterpret_cast<flo
 
 }  // namespace
 
-template <typename T>
+template <typename T, bool DIAG, bool GATES>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                const T* __restrict__ w, const T* __restrict__ b, const T* __restrict__ g,
@@ -91,12 +91,13 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   }
 
   GDN2_TMARK(0);
+  StageDiag dkg, dqg, dsc;   // stage diagnostics (p.diag only)
   // ---- phase 0: gc = in-chunk cumsum of g (gdn2_fwd.py:105-107), kg, qg
 #pragma unroll 8
   for (int it = 0; it < C * D / 4 / kThreads; ++it) {
     const int e = threadIdx.x + it * kThreads;
     const int r = e >> 5, cc = (e & 31) * 4;
-    sts4(sgc + r * GLD + cc, ld4<T>(gcp + r * rs + cc));
+    sts4(sgc + r * GLD + cc, ld4_gate<T>(gcp + r * rs + cc, GATES, kGateG));
   }
   fence_before_sync();
   __syncthreads();
@@ -140,6 +141,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                                      san(kv.z * __expf(l4.z - gi.z), p.clip),
                                      san(kv.w * __expf(l4.w - gi.w), p.clip));
       sts4(kgo + i * D + d, kg4);
+      if (DIAG) dkg.add4(kg4);
       // row L1 norm of kg: the 8 lanes sharing row i cover 32 columns
       float l1 = fabsf(kg4.x) + fabsf(kg4.y) + fabsf(kg4.z) + fabsf(kg4.w);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -150,6 +152,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       tq[(d + 1) * QLD + i] = san(qv.y * __expf(gi.y), p.clip);
       tq[(d + 2) * QLD + i] = san(qv.z * __expf(gi.z), p.clip);
       tq[(d + 3) * QLD + i] = san(qv.w * __expf(gi.w), p.clip);
+      if (DIAG)
+        dqg.add4(make_float4(tq[(d + 0) * QLD + i], tq[(d + 1) * QLD + i], tq[(d + 2) * QLD + i],
+                             tq[(d + 3) * QLD + i]));
     }
     __syncthreads();
     float* qgo = ws.qgT + chunk * C * D;
@@ -159,6 +164,10 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       qgo[e] = tq[(e >> 7) * QLD + (e & 127)];
     }
     __syncthreads();
+    if (DIAG) {
+      dkg.flush(ws.status, kDiagKg);
+      dqg.flush(ws.status, kDiagQg);
+    }
     // max_i ||kg_i||_1, the gain of dv_new's kg dh term (backward guard)
     const float kl1 = block_max(threadIdx.x < C ? ts.rowl1[threadIdx.x] : 0.f, red);
     if (threadIdx.x == 0) ws.bnd[chunk * 4] = kl1;
@@ -194,7 +203,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         const int d = s * KS + cc;
         qx[it] = ld4<T>(qc + i * rs + d);
         kx[it] = ld4<T>(kc + i * rs + d);
-        bx[it] = ld4<T>(bc + i * rs + d);
+        bx[it] = ld4_gate<T>(bc + i * rs + d, GATES, kGateB);
       }
     };
     load_qkb(0, qa, ka, ba);
@@ -259,12 +268,20 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     // 32 consecutive i, coalesced in global memory and conflict-free in S
     for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {   // Aqk / scale
 #pragma unroll
-      for (int t = 0; t < 16; ++t) aqkT[(c + t) * C + i] = c + t <= i ? san(p.scale * v[t], p.clip) : 0.f;
+      for (int t = 0; t < 16; ++t) {
+        aqkT[(c + t) * C + i] = c + t <= i ? san(p.scale * v[t], p.clip) : 0.f;
+        if (DIAG) dsc.add(aqkT[(c + t) * C + i]);
+      }
     });
+    if (DIAG) dsc.flush(ws.status, kDiagAqk);
     for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // S[j][i] = Akk(i, j)
 #pragma unroll
-      for (int t = 0; t < 16; ++t) S[(c + t) * TLD + i] = c + t < i ? san(v[t], p.clip) : 0.f;
+      for (int t = 0; t < 16; ++t) {
+        S[(c + t) * TLD + i] = c + t < i ? san(v[t], p.clip) : 0.f;
+        if (DIAG) dsc.add(S[(c + t) * TLD + i]);
+      }
     });
+    if (DIAG) dsc.flush(ws.status, kDiagAkk);
   } else {
     // exact elementwise form with the +-20 exponent clip (gdn2_fwd.py:124-139)
     for (int e = threadIdx.x; e < C * C; e += kThreads) {
@@ -275,11 +292,19 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           const float ed = __expf(fminf(fmaxf(sgc[i * GLD + d] - sgc[j * GLD + d], -20.f), 20.f));
           const float kj = to_f<T>(kc[j * rs + d]) * ed;
           sq = fmaf(to_f<T>(qc[i * rs + d]), kj, sq);
-          sk = fmaf(to_f<T>(bc[i * rs + d]) * to_f<T>(kc[i * rs + d]), kj, sk);
+          sk = fmaf(ld_gate<T>(bc + i * rs + d, GATES, kGateB) * to_f<T>(kc[i * rs + d]), kj, sk);
         }
       }
       aqkT[j * C + i] = (j <= i) ? san(p.scale * sq, p.clip) : 0.f;
       S[j * TLD + i] = (j < i) ? san(sk, p.clip) : 0.f;
+      if (DIAG) {
+        dsc.add(aqkT[j * C + i]);
+        dqg.add(S[j * TLD + i]);   // (dqg reused as the Akk accumulator here)
+      }
+    }
+    if (DIAG) {
+      dsc.flush(ws.status, kDiagAqk);
+      dqg.flush(ws.status, kDiagAkk);
     }
   }
   __syncthreads();
@@ -289,7 +314,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   wy_inverse_T128(S, TLD, tmp, t0, p.bc, p.clip);
   GDN2_TMARK(4);
   float* at = ws.AT + chunk * C * C;
-  for_tile([&](int j, int i) { sts4(at + j * C + i, lds4(S + j * TLD + i)); });
+  for_tile([&](int j, int i) {
+    const float4 a4 = lds4(S + j * TLD + i);
+    sts4(at + j * C + i, a4);
+    if (DIAG) dsc.add4(a4);
+  });
+  if (DIAG) dsc.flush(ws.status, kDiagA);
   {
     // A (rows i, K = j) split into hi (TMEM 256..383) and lo (384..511): the A
     // operand of phase 3.  S[j * TLD + i] = A(i, j), one TMEM lane per row i.
@@ -323,9 +353,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 #pragma unroll
       for (int jr = 0; jr < 4; ++jr) {
         const int j = sl * KS + kb4 * 4 + jr, d = rb * 4;
-        fb.v[jr] = ld4<T>(bc + j * rs + d);
+        fb.v[jr] = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
         fk.v[jr] = ld4<T>(kc + j * rs + d);
-        fw.v[jr] = ld4<T>(wc + j * rs + d);
+        fw.v[jr] = ld4_gate<T>(wc + j * rs + d, GATES, kGateW);
         fv.v[jr] = ld4<T>(vc + j * rs + d);
       }
     };
@@ -358,14 +388,22 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   float* uo = ws.U + chunk * C * D;
   for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {     // W^T, coalesced per column
 #pragma unroll
-    for (int t = 0; t < 16; ++t) wt[(c + t) * C + i] = san(v[t], p.clip);
+    for (int t = 0; t < 16; ++t) {
+      wt[(c + t) * C + i] = san(v[t], p.clip);
+      if (DIAG) dsc.add(san(v[t], p.clip));
+    }
   });
+  if (DIAG) dsc.flush(ws.status, kDiagW);
   for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // U, one row per lane
 #pragma unroll
-    for (int t = 0; t < 16; t += 4)
-      sts4(uo + i * D + c + t, make_float4(san(v[t], p.clip), san(v[t + 1], p.clip),
-                                           san(v[t + 2], p.clip), san(v[t + 3], p.clip)));
+    for (int t = 0; t < 16; t += 4) {
+      const float4 u4 = make_float4(san(v[t], p.clip), san(v[t + 1], p.clip),
+                                    san(v[t + 2], p.clip), san(v[t + 3], p.clip));
+      sts4(uo + i * D + c + t, u4);
+      if (DIAG) dsc.add4(u4);
+    }
   });
+  if (DIAG) dsc.flush(ws.status, kDiagU);
   GDN2_TMARK(7);
   fence_before_sync();
   __syncthreads();
@@ -389,10 +427,12 @@ cudaError_t launch_tc_fwd_intra(const T* q, const T* k, const T* v, const T* w, 
                 "score ring fits");
   static_assert(smem >= (size_t)C * GLD * sizeof(float) + 2 * 2 * (size_t)SLICE_BYTES,
                 "phase-3 ring fits after the gc tile");
-  cudaError_t e = cudaFuncSetAttribute(k_tc_fwd_intra<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  // per-stage diagnostics are compiled into a second instance of the kernel
+  auto kern = p.diag ? (p.gates ? k_tc_fwd_intra<T, true, true> : k_tc_fwd_intra<T, true, false>)
+                     : (p.gates ? k_tc_fwd_intra<T, false, true> : k_tc_fwd_intra<T, false, false>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k_tc_fwd_intra<T><<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, v, w, b, g, p, ws);
+  kern<<<(unsigned)p.B * p.H * p.nc, kThreads, smem, s>>>(q, k, v, w, b, g, p, ws);
   return cudaGetLastError();
 }
 

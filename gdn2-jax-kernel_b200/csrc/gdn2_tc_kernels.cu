@@ -198,6 +198,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   float smax = 0.f;
   bool flagged = false;
   bool clipped = false;   // the state sanitiser acted (reported for sequence parallelism)
+  StageDiag dhf;          // h_final diagnostics (forward, p.diag only)
 #pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     const int c0 = dcol0 + q * 16;
@@ -295,6 +296,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
         if (!PROD && !(fabsf(pre) <= p.clip)) clipped = true;
         if (kGuard) smax = fmaxf(smax, fabsf(y));
         if (dst) dst[(c0 + j) * D + vrow] = y;
+        if (!BWD && !PROD && last && p.diag) dhf.add(y);
         if (BWD && last && out_final) out_final[bh * D * D + (c0 + j) * D + vrow] = san(y, 1e4f);
         split(y, hv[j], lv[j]);
       }
@@ -306,6 +308,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   }
   if (kGuard && threadIdx.x == 0) ws.bnd[bh * p.nc * 4 + 3] = flagged ? 1.f : 0.f;
   if (clipped) atomicOr(ws.status + (BWD ? 2 : 1), 1);
+  if (!BWD && !PROD && p.diag && out_final) dhf.flush(ws.status, kDiagHFinal);
   if (kGuard && flagged && threadIdx.x == 0) atomicOr(ws.status + 3, 1);
   fence_before_sync();
   __syncthreads();
@@ -376,12 +379,17 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   if (o) {
     const long rs = p.row_stride();
     float* orow = o + ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
+    StageDiag dg;
     for_acc<128>(tmem, 128, [&](int i, int c0, const float* x) {
 #pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        st4f(orow + i * rs + c0 + j, make_float4(san(x[j], p.clip), san(x[j + 1], p.clip),
-                                                 san(x[j + 2], p.clip), san(x[j + 3], p.clip)));
+      for (int j = 0; j < 16; j += 4) {
+        const float4 o4 = make_float4(san(x[j], p.clip), san(x[j + 1], p.clip),
+                                      san(x[j + 2], p.clip), san(x[j + 3], p.clip));
+        st4f(orow + i * rs + c0 + j, o4);
+        if (p.diag) dg.add4(o4);
+      }
     });
+    if (p.diag) dg.flush(ws.status, kDiagO);
   }
   tc_teardown(tmem, 256);
 }

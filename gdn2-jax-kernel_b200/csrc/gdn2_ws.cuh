@@ -12,6 +12,8 @@ namespace gdn2 {
 struct Problem {
   int B, T, H, D, C, nc;   // C = chunk length BT, nc = T / C
   int bc;                  // the reference's sub-block BC (clip granularity of B4)
+  int diag;                // 1: accumulate per-stage diagnostics in the status header
+  int gates;               // 1: w, b, g are pre-activations (GDN2_GATES_RAW)
   float scale, clip;
   __host__ __device__ long row_stride() const { return (long)H * D; }
 };

@@ -13,6 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libgdn2.so")
 
 F32, BF16 = 0, 1
+GATES_RAW = 0x100   # flag OR-ed into the dtype code (include/gdn2.h)
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA = 0, -1, -2, -3
 # bits of gdn2_workspace_status (include/gdn2.h)
 STATUS_WAIT_TIMEOUT, STATUS_FWD_STATE_CLIPPED, STATUS_BWD_STATE_CLIPPED = 1, 2, 4
@@ -40,7 +41,27 @@ SIGNATURES = {
     "gdn2_workspace_status": (_i, [_vp, _sz, _vp]),
     "gdn2_noalloc_status": (_i, [_vp]),
     "gdn2_selftest_wait_timeout": (_i, [_vp, _sz, _i, _vp]),
+    "gdn2_diag_enable": (_i, [_i]),
+    "gdn2_diag_read": (_i, [_vp, _sz, _vp, _i, ctypes.POINTER(ctypes.c_int),
+                            ctypes.POINTER(ctypes.c_float)]),
 }
+
+# Stage tags of the forward diagnostics, in gdn2_diag_read's order
+# (the reference's _stage_diag tags, gdn2_fwd.py:407-417, 360-363).
+DIAG_STAGES = ("kernel_A_Aqk", "kernel_A_Akk", "kernel_B_wy_inverse_A", "kernel_C_w_pseudo",
+               "kernel_C_u", "kernel_C_kg", "kernel_C_qg", "kernel_D_o", "kernel_D_h_final")
+
+
+def diag_read(ws, stream):
+    """{stage tag: (n_nonfinite, max_abs)} of the latest forward on ``ws``
+    (diagnostics must have been enabled for that call).  Synchronizes."""
+    n = len(DIAG_STAGES)
+    nf = (ctypes.c_int * n)()
+    mx = (ctypes.c_float * n)()
+    rc = load().gdn2_diag_read(ws.data_ptr(), ws.numel(), stream, n, nf, mx)
+    if rc < 0:
+        check(rc, "gdn2_diag_read")
+    return {t: (nf[i], mx[i]) for i, t in enumerate(DIAG_STAGES)}
 
 STAGES = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra1", "bwd_intra2", "bwd_intra3",
           "fwd_affine", "fwd_scan", "fwd_out", "bwd_prep", "bwd_scan", "bwd_exact")

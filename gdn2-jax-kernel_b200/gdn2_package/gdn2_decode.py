@@ -37,7 +37,10 @@ def gdn2_decode(q, k, v, w, b, g, scale, h0=None):
             raise _fwd.Gdn2ShapeError(f"h0 must be {(B, H, D, D)}; got {tuple(hs.shape)}")
     o = torch.empty((B, T, H, D), dtype=torch.float32, device=dev)
     hf = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
-    rc = _lib.load().gdn2_decode(_lib.F32 if cdt == torch.float32 else _lib.BF16,
+    code = _lib.F32 if cdt == torch.float32 else _lib.BF16
+    if _fwd.GATES == "raw":
+        code |= _lib.GATES_RAW
+    rc = _lib.load().gdn2_decode(code,
                                  *[t.data_ptr() for t in x],
                                  hs.data_ptr() if hs is not None else None, o.data_ptr(),
                                  hf.data_ptr(), B, T, H, D, float(scale), float(_fwd.CLIP),

@@ -42,6 +42,13 @@ EXACT_BT = True
 # every output and gradient of the real tokens unchanged, and slices back.
 MASKED_TAIL = False
 
+# Gate inputs.  "activated" (the reference's contract, README.md:60-68): the
+# caller passes w = sigmoid(.), b = sigmoid(.), g = -softplus(.).  "raw": the
+# caller passes the pre-activations, the kernels apply the activations as
+# they load w, b, g (no separate pass over them), and the backward returns
+# gradients with respect to the pre-activations.
+GATES = "activated"
+
 _GDN2_FWD_DIAG = os.environ.get("GDN2_FWD_DIAG", "0") == "1"
 _KERNEL_CHUNKS = (128, 64)
 _SUPPORTED_D = (64, 128)
@@ -68,18 +75,43 @@ def _kernel_chunk(T, bt, D):
     raise Gdn2ShapeError(f"BT={bt} unsupported: kernels run chunks of 128 or 64")
 
 
+_LARGE_THRESHOLD = 1e6   # gdn2_fwd.py:38
+
+
+def _diag_line(tag, n_bad, mx):
+    """The reference's two reports (gdn2_fwd.py:56-69), or None."""
+    if n_bad:
+        return f"[GDN2-FWD-DIAG] non-finite at {tag}: n_nonfinite={n_bad} max_abs={mx:.3e}"
+    if mx > _LARGE_THRESHOLD:
+        return f"[GDN2-FWD-DIAG] large value at {tag}: max_abs={mx:.3e}"
+    return None
+
+
 def _stage_diag(tag, x):
-    """Non-finite / large-value report when GDN2_FWD_DIAG=1 (gdn2_fwd.py:47-76)."""
+    """Non-finite / large-value report of one tensor when GDN2_FWD_DIAG=1
+    (gdn2_fwd.py:47-76); returns x."""
     if not _GDN2_FWD_DIAG:
         return x
     finite = torch.isfinite(x)
     n_bad = int((~finite).sum())
     mx = float(torch.where(finite, x, torch.zeros_like(x)).abs().max()) if x.numel() else 0.0
-    if n_bad:
-        print(f"[GDN2-FWD-DIAG] non-finite at {tag}: n_nonfinite={n_bad} max_abs={mx:.3e}")
-    elif mx > 1e6:
-        print(f"[GDN2-FWD-DIAG] large value at {tag}: max_abs={mx:.3e}")
+    line = _diag_line(tag, n_bad, mx)
+    if line:
+        print(line)
     return x
+
+
+def _stage_reports(debug_tag, ws, stream):
+    """Per-stage reports of the forward that just ran on ``ws``, from the
+    counters its kernels accumulated on the device (every stage the
+    reference's gdn2_pallas_forward checks, gdn2_fwd.py:407-417, 360-363)."""
+    lines = []
+    for tag, (n_bad, mx) in _lib.diag_read(ws, stream).items():
+        line = _diag_line(f"{debug_tag}:{tag}", n_bad, mx)
+        if line:
+            lines.append(line)
+            print(line)
+    return lines
 
 
 class _Prepared:
@@ -127,6 +159,10 @@ class _Prepared:
         self.dev = dev
         self.dtype = cdt
         self.code = _lib.F32 if cdt == torch.float32 else _lib.BF16
+        if GATES not in ("activated", "raw"):
+            raise Gdn2ShapeError(f"GATES={GATES!r}: 'activated' or 'raw'")
+        if GATES == "raw":
+            self.code |= _lib.GATES_RAW
         self.t = tuple(t.to(device=dev, dtype=cdt, non_blocking=True).contiguous() for t in ts)
         if T != self.T_user:
             self.t = tuple(self.pad(t) for t in self.t)
@@ -162,8 +198,9 @@ class _Prepared:
         return torch.empty(n, dtype=torch.uint8, device=self.dev)
 
 
-def _run_forward(p, save_residuals=False, ws=None):
+def _run_forward(p, save_residuals=False, ws=None, debug_tag=""):
     lib = _lib.load()
+    lib.gdn2_diag_enable(int(_GDN2_FWD_DIAG))
     o = torch.empty((p.B, p.T, p.H, p.D), dtype=torch.float32, device=p.dev)
     h_final = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
     if ws is None:
@@ -174,6 +211,8 @@ def _run_forward(p, save_residuals=False, ws=None):
                       p.stream)
     _lib.check(rc, "gdn2_fwd")
     _lib.check_status(ws, p.stream, "gdn2_fwd", synced=p.on_host)
+    if _GDN2_FWD_DIAG:
+        _stage_reports(debug_tag, ws, p.stream)
     return p.unpad(o), h_final, ws
 
 
@@ -181,9 +220,7 @@ def gdn2_pallas_forward(q, k, v, w, b, g, scale, h0=None, debug_tag=""):
     """Full forward: Kernels A -> B -> C -> D.  Returns o (B,T,H,D) float32
     and h_final (B,H,D,D) float32 (gdn2_fwd.py:400-424)."""
     p = _Prepared(q, k, v, w, b, g, scale, h0)
-    o, h_final, _ = _run_forward(p)
-    o = _stage_diag(f"{debug_tag}:kernel_D_o", o)
-    h_final = _stage_diag(f"{debug_tag}:kernel_D_h_final", h_final)
+    o, h_final, _ = _run_forward(p, debug_tag=debug_tag)
     if p.on_host:
         return o.cpu(), h_final.cpu()
     return o, h_final
@@ -220,7 +257,7 @@ def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_t
     the batch-major (B, H, nc, ...) layout the backward consumes.  The
     reference additionally returns Akk, which the fused kernels never store."""
     p = _Prepared(q, k, v, w, b, g, scale, h0)
-    o, h_final, ws = _run_forward(p, save_residuals=True)
+    o, h_final, ws = _run_forward(p, save_residuals=True, debug_tag=debug_tag)
     res = {n: t.clone() for n, t in _unpack_residuals(p, ws).items()}
     if p.on_host:
         return o.cpu(), h_final.cpu(), {n: t.cpu() for n, t in res.items()}

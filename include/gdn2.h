@@ -32,6 +32,13 @@ extern "C" {
 #define GDN2_ABI_VERSION 1
 
 enum { GDN2_F32 = 0, GDN2_BF16 = 1 };
+/* OR-ed into the dtype argument of gdn2_fwd / gdn2_bwd / gdn2_fwd_noalloc /
+ * gdn2_decode: w, b, g are pre-activations and the kernels apply
+ * w = sigmoid(w), b = sigmoid(b), g = -softplus(g) as they load them (the
+ * activations the reference leaves to its caller, README.md:60-68).
+ * gdn2_bwd then returns dw, db, dg with respect to the pre-activations.  The
+ * same flag must be given to the forward and the backward of one step. */
+#define GDN2_GATES_RAW 0x100
 enum {
   GDN2_OK = 0,
   GDN2_ERR_INVALID = -1,   /* bad shape / argument (reference: AssertionError, gdn2_fwd.py:145-146) */
@@ -109,6 +116,19 @@ int gdn2_sp_segment(int op, void* workspace, size_t workspace_bytes, const float
 #define GDN2_STATUS_EXACT_RECOMPUTE 8
 #define GDN2_STATUS_B4_EXACT 16
 int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-stage diagnostics of the forward (the reference's _stage_diag,
+ * gdn2_fwd.py:47-76, enabled there by GDN2_FWD_DIAG=1).  While enabled
+ * (process-wide), every forward kernel reduces, for each stage output, the
+ * number of non-finite values and the largest finite |x| into the status
+ * header of its workspace.  gdn2_diag_read() copies them to the host
+ * (synchronizing `stream`) for stages 0 kernel_A_Aqk, 1 kernel_A_Akk,
+ * 2 kernel_B_wy_inverse_A, 3 kernel_C_w_pseudo, 4 kernel_C_u, 5 kernel_C_kg,
+ * 6 kernel_C_qg, 7 kernel_D_o, 8 kernel_D_h_final and returns the number of
+ * stages (9).  Values describe the latest call on that workspace. */
+int gdn2_diag_enable(int on);
+int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
+                   int* nonfinite, float* maxabs);
 
 /* Forward for callers that cannot allocate device memory (no counterpart in
  * the reference).  Same arguments and results as gdn2_fwd without the

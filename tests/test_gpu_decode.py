@@ -54,3 +54,37 @@ def test_decode_rejects_bad_shapes():
     x = torch.zeros((1, 4, 2, 96), device="cuda")
     with pytest.raises(ValueError):
         gdn2_decode(x, x, x, x, x, x, 0.1)
+
+
+@pytest.mark.parametrize("clip,gscale", [(0.3, 1.0), (1e4, 30.0)])
+def test_decode_is_the_one_token_chunked_form(clip, gscale, monkeypatch):
+    """Every sanitiser of the chunked form acts per token (W, U, kg, qg,
+    gc_last, Aqk, o, h): equal to the oracle's chunked forward with BT = BC
+    = 1, also with CLIP acting and with fast-decaying gates (g x 30, which
+    exercise the exponential over its range)."""
+    monkeypatch.setattr(gdn2_fwd, "CLIP", clip)
+    inp = make_inputs(2, 24, 2, 128, seed=33, h0_std=0.1, grads=False)
+    inp["g"] = inp["g"] * np.float32(gscale)
+    args = [torch.as_tensor(inp[n]).cuda() for n in NAMES]
+    o, h = gdn2_decode(*args, inp["scale"], torch.as_tensor(inp["h0"]).cuda())
+    o_r, h_r = O.forward(*[inp[n].astype(np.float64) for n in NAMES], inp["scale"], inp["h0"],
+                         1, 1, clip)
+    assert rel(o, o_r) < 1e-5 and rel(h, h_r) < 1e-5, (rel(o, o_r), rel(h, h_r))
+
+
+def test_decode_with_raw_gates(monkeypatch):
+    """GATES = "raw": sigmoid / -softplus applied in the kernel equal the
+    activations applied by the caller."""
+    inp = make_inputs(1, 8, 2, 64, seed=34, h0_std=0.1, grads=False)
+    raw = {n: torch.randn(inp[n].shape, generator=torch.Generator().manual_seed(i))
+           for i, n in enumerate(("w", "b", "g"))}
+    act = dict(w=torch.sigmoid(raw["w"]), b=torch.sigmoid(raw["b"]),
+               g=-torch.nn.functional.softplus(raw["g"]))
+    base = [torch.as_tensor(inp[n]) for n in ("q", "k", "v")]
+    h0 = torch.as_tensor(inp["h0"]).cuda()
+    o_a, h_a = gdn2_decode(*[t.cuda() for t in base + [act["w"], act["b"], act["g"]]],
+                           inp["scale"], h0)
+    monkeypatch.setattr(gdn2_fwd, "GATES", "raw")
+    o_r, h_r = gdn2_decode(*[t.cuda() for t in base + [raw["w"], raw["b"], raw["g"]]],
+                           inp["scale"], h0)
+    assert rel(o_r, o_a.double().cpu().numpy()) < 1e-5 and rel(h_r, h_a.double().cpu().numpy()) < 1e-5

@@ -390,3 +390,72 @@ def test_streamed_host_batches_equal_device_call(dtype, backward):
             assert torch.equal(a, b.cpu())
     else:
         assert g is None
+
+
+@pytest.mark.parametrize("BT,BC", [(128, 64), (64, 16)])
+def test_stage_diagnostics_from_device_counters(BT, BC, monkeypatch, capsys):
+    """GDN2_FWD_DIAG: every stage output the reference checks
+    (gdn2_fwd.py:407-417) is reduced on the device.  Large values (v x 1e7,
+    CLIP 1e9) are reported at kernel_C_u / kernel_D_h_final with the maxima of the
+    stored tensors; an infinite q with CLIP = inf is reported non-finite at
+    kernel_C_qg (qg = q e^gc keeps it)."""
+    from gdn2_package import _lib
+    monkeypatch.setattr(gdn2_fwd, "_GDN2_FWD_DIAG", True)
+    _set_consts(BT, BC, 1e9)
+    inp = make_inputs(1, 256, 2, 128, seed=23, h0_std=0.1, grads=False)
+    inp["v"] = inp["v"] * np.float32(1e7)
+    args = _dev(inp, torch.float32)
+    o, h, res = gdn2_pallas_forward_with_residuals(*args, inp["scale"],
+                                                   torch.as_tensor(inp["h0"]).cuda(),
+                                                   debug_tag="t")
+    out = capsys.readouterr().out
+    assert "large value at t:kernel_C_u" in out and "large value at t:kernel_D_h_final" in out, out
+    assert "t:kernel_A_Aqk" not in out and "non-finite" not in out, out
+    from gdn2_package.gdn2_fwd import _Prepared, _run_forward
+    p = _Prepared(*args, inp["scale"], torch.as_tensor(inp["h0"]).cuda())
+    o2, h2, ws = _run_forward(p, save_residuals=True, debug_tag="t")
+    stats = _lib.diag_read(ws, p.stream)
+    for tag, t in (("kernel_C_u", res["u"]), ("kernel_D_o", o2), ("kernel_D_h_final", h2),
+                   ("kernel_A_Aqk", res["Aqk"]), ("kernel_C_kg", res["kg"])):
+        assert stats[tag][0] == 0 and stats[tag][1] == float(t.abs().max()), (tag, stats[tag])
+    capsys.readouterr()
+    _set_consts(BT, BC, float("inf"))
+    inp2 = make_inputs(1, 256, 2, 128, seed=24, grads=False)
+    inp2["q"][0, 5, 1, 3] = np.inf
+    gdn2_pallas_forward(*_dev(inp2, torch.float32), inp2["scale"], debug_tag="u")
+    out = capsys.readouterr().out
+    assert "non-finite at u:kernel_C_qg" in out, out
+
+
+@pytest.mark.parametrize("BT,BC,dtype", [(128, 64, torch.float32), (64, 16, torch.float32),
+                                         (128, 64, torch.bfloat16)])
+def test_raw_gates_fused_into_the_loads(BT, BC, dtype, monkeypatch):
+    """GATES = "raw": the kernels apply w = sigmoid(w'), b = sigmoid(b'),
+    g = -softplus(g') as they load them, and return dw', db', dg'.  Checked
+    against the float64 oracle on the activated inputs, with the chain rule
+    applied to its gradients."""
+    _set_consts(BT, BC, 1e3)
+    inp = make_inputs(2, 256, 2, 128, seed=41, h0_std=0.1)
+    rng = np.random.default_rng(5)
+    raw = {n: rng.standard_normal(inp[n].shape).astype(np.float32) for n in ("w", "b", "g")}
+    xs = dict(inp, **raw)
+    args = [torch.as_tensor(xs[n]).cuda().to(dtype) for n in NAMES]
+    h0 = torch.as_tensor(inp["h0"]).cuda()
+    monkeypatch.setattr(gdn2_fwd, "GATES", "raw")
+    o, h = gdn2_pallas_forward(*args, inp["scale"], h0)
+    grads = gdn2_backward(*args, inp["scale"], h0, torch.as_tensor(inp["dout"]).cuda(),
+                          torch.as_tensor(inp["dh_final"]).cuda())
+    r = {n: torch.as_tensor(xs[n]).to(dtype).double().numpy() for n in NAMES}
+    sig = lambda x: 1.0 / (1.0 + np.exp(-x))
+    act = dict(r, w=sig(r["w"]), b=sig(r["b"]), g=-np.logaddexp(0.0, r["g"]))
+    ref_in = [act[n] for n in NAMES]
+    o_r, h_r = O.forward(*ref_in, inp["scale"], inp["h0"], BT, BC, 1e3)
+    tol = TOL[dtype]
+    assert rel(o, o_r) < tol and rel(h, h_r) < tol, (rel(o, o_r), rel(h, h_r))
+    g_r = list(O.backward(*ref_in, inp["scale"], inp["h0"], inp["dout"], inp["dh_final"], BT, BC,
+                          1e3))
+    g_r[3] = g_r[3] * act["w"] * (1 - act["w"])          # dw'
+    g_r[4] = g_r[4] * act["b"] * (1 - act["b"])          # db'
+    g_r[5] = g_r[5] * -sig(r["g"])                        # dg'
+    for name, a, b in zip(GRADS, grads, g_r):
+        assert rel(a, b) < tol, (name, rel(a, b))
