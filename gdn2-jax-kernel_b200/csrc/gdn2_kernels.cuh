@@ -276,6 +276,8 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
   constexpr int C = 128, H = 64, LY = 68;
 #ifdef GDN2_PHASE_TIMING
   long long t0 = clock64();
+  long long wy_t[2];
+  (void)wy_t;
 #endif
   wy_micro_solves<C>(S, ld, clip);
 #ifdef GDN2_PHASE_TIMING
@@ -285,8 +287,7 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
   else if (bc > 16) wy_compose_seq<16>(S, ld, C, bc / 16, tmp, clip);   // inside each sub-block
 #ifdef GDN2_PHASE_TIMING
   long long t2 = clock64();
-  if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
-    printf("wy phases: micro %lld level1 %lld\n", t1 - t0, t2 - t1);
+  if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) wy_t[0] = t1 - t0, wy_t[1] = t2 - t1;
 #endif
   if (bc != 64) {
     if (C > bc) wy_compose_blocks(S, ld, C, bc, C / bc, tmp, clip);

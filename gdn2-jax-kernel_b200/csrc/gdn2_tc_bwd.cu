@@ -126,7 +126,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   {
     const float dclip = (c + 1 < p.nc) ? 0.f : p.clip;
     const Src srcs[2] = {direct(ws.kg + chunk * C * D, D), trans(dhn, D, 1.f, dclip)};   // (i,d), (v,d)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
     });
   }
@@ -161,7 +161,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   // contraction over the value dim v for every product
   {
     const Src srcs[2] = {direct(doc, rs), direct(hpre, D)};  // (i,v) (dk,v)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);
       mma3_ta(tmem + 128, tmem + 256 + s * KS, tmem + 384 + s * KS, ring.op(buf, 1), 128, KS / 8,
               s > 0);
@@ -171,7 +171,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   ring.nop = 3;
   {
     const Src srcs[3] = {direct(vnew, D), direct(doc, rs), direct(dhn, D)};  // (i|j,v) (i,v) (dk,v)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);
       mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);
     });
@@ -539,6 +539,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       if (pass > 0) GDN2_TMARK(1 + 2 * pass);
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
       const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
+#pragma unroll 1
       for (int sl = 0; sl < 4; ++sl, ++gs) {
         const int J = sl * 32 / JW, r = JW * J, k0 = 32 * sl;   // K slice k0 of block J
         const int buf = gs & 1;

@@ -60,7 +60,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   extern __shared__ __align__(128) float sm[];
   __shared__ __align__(16) TcSmemF ts;
 #ifdef GDN2_PHASE_TIMING
-  long long tmark[8];
+  long long tmark[16];
 #endif
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % p.nc);
@@ -102,11 +102,14 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  GDN2_TMARK(8);
   const uint32_t tmem = ts.tmem;
   float gpos = -1.f;
   for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[(e / D) * GLD + e % D]);
   const float gmax = block_max(gpos, red);
+  GDN2_TMARK(9);
   column_cumsum<C, D, GLD>(sgc, red);
+  GDN2_TMARK(10);
   // largest decay-block width (64 or 32 rows) whose in-block gc spread keeps
   // every factor e^{gc_r - gc_j} inside the float range
   float spread = 0.f, spread64 = 0.f;
@@ -117,10 +120,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   }
   const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
   const int JW = block_max(spread64, red) <= 80.f ? 64 : 32;
+  GDN2_TMARK(11);
   {
     float* gco = ws.gc + chunk * C * D;
     for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4)
       sts4(gco + e, lds4(sgc + (e / D) * GLD + e % D));
+    GDN2_TMARK(12);
     if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * GLD + threadIdx.x], p.clip);
     float* kgo = ws.kg + chunk * C * D;
     const float* gl = sgc + (C - 1) * GLD;
@@ -157,6 +162,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                              tq[(d + 3) * QLD + i]));
     }
     __syncthreads();
+    GDN2_TMARK(13);
     float* qgo = ws.qgT + chunk * C * D;
 #pragma unroll 8
     for (int it = 0; it < C * D / kThreads; ++it) {
@@ -207,15 +213,14 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       }
     };
     load_qkb(0, qa, ka, ba);
-#pragma unroll
+    // rolled slice loop (instruction-cache friendly); the prefetched slice is
+    // copied into the current registers at the end of each step
+#pragma unroll 1
     for (int s = 0; s < D / KS; ++s) {
-      float4* qx = (s & 1) ? qn : qa;
-      float4* kx = (s & 1) ? kn : ka;
-      float4* bx = (s & 1) ? bn : ba;
-      if (s + 1 < D / KS) {
-        if (s & 1) load_qkb(s + 1, qa, ka, ba);
-        else load_qkb(s + 1, qn, kn, bn);
-      }
+      const float4* qx = qa;
+      const float4* kx = ka;
+      const float4* bx = ba;
+      if (s + 1 < D / KS) load_qkb(s + 1, qn, kn, bn);
 #pragma unroll 1
       for (int J = 0; J < C / JW; ++J, ++gs) {
         const int r = JW * J;
@@ -260,6 +265,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           if (who == kIss - 1) mma3(tmem + 128 + r, ring.op(buf, 1), B, JW, KS / 8, s > 0);
           commit(&ring.bars[buf]);
         }
+      }
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        qa[it] = qn[it];
+        ka[it] = kn[it];
+        ba[it] = bn[it];
       }
     }
   GDN2_TMARK(2);
@@ -411,9 +422,11 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   if ((threadIdx.x >> 5) == 0) tmem_free(tmem, 512);
 #ifdef GDN2_PHASE_TIMING
   if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
-    printf("fwd_intra phases: %lld %lld %lld %lld %lld %lld %lld\n", tmark[1] - tmark[0],
-           tmark[2] - tmark[1], tmark[3] - tmark[2], tmark[4] - tmark[3], tmark[5] - tmark[4],
-           tmark[6] - tmark[5], tmark[7] - tmark[6]);
+    printf("fwd_intra phases: %lld %lld %lld %lld %lld %lld %lld | p0: %lld %lld %lld %lld %lld %lld %lld\n",
+           tmark[1] - tmark[0], tmark[2] - tmark[1], tmark[3] - tmark[2], tmark[4] - tmark[3],
+           tmark[5] - tmark[4], tmark[6] - tmark[5], tmark[7] - tmark[6], tmark[8] - tmark[0],
+           tmark[9] - tmark[8], tmark[10] - tmark[9], tmark[11] - tmark[10],
+           tmark[12] - tmark[11], tmark[13] - tmark[12], tmark[1] - tmark[13]);
 #endif
 }
 

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   const float* u = ws.U + chunk * C * D;
   int g = 0;
   const Src srcs[3] = {trans(kg, D), direct(wt, C), trans(u, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
-  kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+  kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
     mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);         // kg^T W
     mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);   // kg^T U
     mma3(tmem + 256, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);   // (kg^T W)^T
@@ -336,7 +336,7 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   int g = 0;
   {
     const Src srcs[3] = {trans(wt, C), trans(qgt, C, p.scale), trans(hp, D)};  // W, s qg, h^T
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // (W h)^T: (v, i)
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg h: (i, v)
     });
@@ -370,7 +370,7 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   ring.nop = 1;
   {
     const Src srcs[1] = {trans(aqkt, C)};   // (i,j) = Aqk
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       float* hi = vt + s * 2 * SLICE_FLOATS;
       mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, 1);
     });
@@ -416,7 +416,7 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   int g = 0;
   {
     const Src srcs[3] = {direct(aqkt, C), direct(qgt, C, p.scale), trans(doc, rs)};  // (j,i) (d,i) (v,i)
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // dvp^T: (v, j)
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg^T do
     });
@@ -451,7 +451,7 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   ring.nop = 1;
   {
     const Src srcs[1] = {direct(wt, C, -1.f)};   // (d,j) = -W
-    kloop_pf(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       float* hi = dt + s * 2 * SLICE_FLOATS;
       mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, 1);
     });

@@ -225,9 +225,12 @@ __device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, co
 // loads of slice s+1 are in flight while slice s is split, stored and issued.
 // Operand slot o of the ring holds source o; extra(buf, s) may stage more
 // slots synchronously (e.g. products of several input tensors).
+// The slice loop is rolled (one copy of its body: the kernels run each K loop
+// once per chunk, so unrolled copies cost instruction-cache misses); the
+// register double buffer advances by copying the prefetched slice.
 template <int NOP, class Ex, class Is>
-__device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src (&src)[NOP],
-                                         Ex extra, Is issue) {
+__device__ __forceinline__ void kloop_pf_unrolled(Ring& ring, int& g, int* err,
+                                                  const Src (&src)[NOP], Ex extra, Is issue) {
   Frag fa[NOP], fb[NOP];
 #pragma unroll
   for (int o = 0; o < NOP; ++o) src_load(src[o], 0, fa[o]);
@@ -250,6 +253,41 @@ __device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src
       commit(&ring.bars[buf]);
     }
     ++g;
+  }
+}
+
+// ROLL = false: the slice loop fully unrolled (measured faster for the short
+// kernels whose K loops carry few operands: affine, fwd_out, bwd_prep, and the
+// dv / dqg loops of bwd_intra1).
+template <bool ROLL = true, int NOP, class Ex, class Is>
+__device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src (&src)[NOP],
+                                         Ex extra, Is issue) {
+  if (!ROLL) {
+    kloop_pf_unrolled(ring, g, err, src, extra, issue);
+    return;
+  }
+  Frag cur[NOP], nxt[NOP];
+#pragma unroll
+  for (int o = 0; o < NOP; ++o) src_load(src[o], 0, cur[o]);
+#pragma unroll 1
+  for (int s = 0; s < 128 / KS; ++s) {
+    if (s + 1 < 128 / KS) {
+#pragma unroll
+      for (int o = 0; o < NOP; ++o) src_load(src[o], (s + 1) * KS, nxt[o]);
+    }
+    const int buf = g & 1;
+    ring_acquire(ring, buf, g >> 1, err);
+#pragma unroll
+    for (int o = 0; o < NOP; ++o) src_store(src[o], ring.hi(buf, o), ring.lo(buf, o), cur[o]);
+    extra(buf, s);
+    slice_publish();
+    if (threadIdx.x == 0) {
+      issue(buf, s);
+      commit(&ring.bars[buf]);
+    }
+    ++g;
+#pragma unroll
+    for (int o = 0; o < NOP; ++o) cur[o] = nxt[o];
   }
 }
 // kloop_pf with the MMA issue split over NISS issuing threads (lane 0 of
@@ -287,7 +325,7 @@ __device__ __forceinline__ void kloop_pf_n(Ring& ring, int& g, int* err, const S
 // sources), with the issue split as in kloop_pf_n.
 template <int NISS, class St, class Is>
 __device__ __forceinline__ void kloop_n(Ring& ring, int& g, int* err, St stage, Is issue) {
-#pragma unroll
+#pragma unroll 1
   for (int s = 0; s < 128 / KS; ++s) {
     const int buf = g & 1;
     ring_acquire(ring, buf, g >> 1, err);
