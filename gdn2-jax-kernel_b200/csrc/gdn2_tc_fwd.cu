@@ -99,6 +99,25 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     const int r = e >> 5, cc = (e & 31) * 4;
     sts4(sgc + r * GLD + cc, ld4_gate<T>(gcp + r * rs + cc, GATES, kGateG));
   }
+  // k and q for the kg / qg pass, four iterations per batch: the first batch
+  // is in flight during the cumsum, each later one during the batch before
+  auto kq_at = [&](int it, int& i, int& d) {
+    const int e = threadIdx.x + it * kThreads;
+    const int l = e & 31, wq = e >> 5;
+    i = (wq & 31) * 4 + (l >> 3);
+    d = ((wq >> 5) * 8 + (l & 7)) * 4;
+  };
+  float4 kcur[4], qcur[4], knx[4], qnx[4];
+  auto ld_kq = [&](int bt, float4* kx, float4* qx) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int i, d;
+      kq_at(4 * bt + u, i, d);
+      kx[u] = ld4<T>(kc + i * rs + d);
+      qx[u] = ld4<T>(qc + i * rs + d);
+    }
+  };
+  ld_kq(0, kcur, qcur);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -134,12 +153,15 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     // global rows are read in 128-byte pieces.
     constexpr int QLD = C + 1;
     float* tq = sm + C * GLD;   // free until the score products start
-#pragma unroll 4
-    for (int it = 0; it < C * D / 4 / kThreads; ++it) {
-      const int e = threadIdx.x + it * kThreads;
-      const int l = e & 31, wq = e >> 5;
-      const int i = (wq & 31) * 4 + (l >> 3), d = ((wq >> 5) * 8 + (l & 7)) * 4;
-      const float4 kv = ld4<T>(kc + i * rs + d), qv = ld4<T>(qc + i * rs + d);
+#pragma unroll 1
+    for (int bt = 0; bt < C * D / 16 / kThreads; ++bt) {
+    if (bt + 1 < C * D / 16 / kThreads) ld_kq(bt + 1, knx, qnx);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int l = threadIdx.x & 31;
+      int i, d;
+      kq_at(4 * bt + u, i, d);
+      const float4 kv = kcur[u], qv = qcur[u];
       const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(gl + d);
       const float4 kg4 = make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
                                      san(kv.y * __expf(l4.y - gi.y), p.clip),
@@ -160,6 +182,12 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       if (DIAG)
         dqg.add4(make_float4(tq[(d + 0) * QLD + i], tq[(d + 1) * QLD + i], tq[(d + 2) * QLD + i],
                              tq[(d + 3) * QLD + i]));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      kcur[u] = knx[u];
+      qcur[u] = qnx[u];
+    }
     }
     __syncthreads();
     GDN2_TMARK(13);
@@ -228,6 +256,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         ring_acquire(ring, buf, gs >> 1, ws.status);
         float* bhi = bsl + buf * 2 * 64 * KS;
         float* blo = bhi + 64 * KS;
+        // Both operands from the slice already in registers: the row operands
+        // for rows i >= r, and the column operand B_J(i - r) = k_i e^{gc_r - gc_i}
+        // for the rows i of block J (the same elements, so no second load).
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
           int i, cc;
@@ -241,21 +272,13 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
             const float4 qv = qx[it], kv = kx[it], bv = bx[it];
             aq = make_float4(qv.x * e0, qv.y * e1, qv.z * e2, qv.w * e3);
             ak = make_float4(bv.x * kv.x * e0, bv.y * kv.y * e1, bv.z * kv.z * e2, bv.w * kv.w * e3);
+            if (i < r + JW)
+              st_split4(bhi, blo, i - r, cc, KS,
+                        make_float4(kv.x * __expf(gr.x - gi.x), kv.y * __expf(gr.y - gi.y),
+                                    kv.z * __expf(gr.z - gi.z), kv.w * __expf(gr.w - gi.w)));
           }
           st_split4(ring.hi(buf, 0), ring.lo(buf, 0), i, cc, KS, aq);
           st_split4(ring.hi(buf, 1), ring.lo(buf, 1), i, cc, KS, ak);
-        }
-        for (int jb = 0; jb < JW; jb += 32) {
-          // 8 consecutive rows per quarter-warp: 8 distinct bank quads
-          const int t = threadIdx.x;
-          const int jj = jb + (t & 7) + 8 * ((t >> 5) & 3), cc = 4 * ((t >> 3) & 3) + 16 * (t >> 7);
-          const int d = s * KS + cc;
-          const int j = r + jj;
-          const float4 gj = lds4(sgc + j * GLD + d), gr = lds4(sgc + r * GLD + d);
-          const float4 kv = ld4<T>(kc + j * rs + d);
-          st_split4(bhi, blo, jj, cc, KS,
-                    make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
-                                kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w)));
         }
         slice_publish();
         if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < kIss) {
