@@ -121,8 +121,8 @@ def step_work(cfg):
 # DRAM bytes (read + write) per chunk of config 1's kernels from one ncu
 # capture at B=1 (384 chunks, inputs larger than L2); traffic grows with the
 # chunk count, so a full launch moves this figure x 3072 chunks.
-NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 743_297, "bwd_intra1": 970_652, "bwd_intra2": 1_199_843,
-                         "bwd_intra3": 952_852}
+NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 738_587, "bwd_intra1": 960_509, "bwd_intra2": 1_199_761,
+                         "bwd_intra3": 944_667}
 
 
 class ClockSampler:
