@@ -15,9 +15,10 @@ of its (batch, head) units (``--scaling strong``); ``value`` is the tokens of
 all ranks / the slowest rank's time.  ``--mode sp`` runs config 3 with the
 sequence split over the ranks.
 
-``--impl reference`` times the CPU restatement of the reference algorithm
-(oracle/gdn2_oracle.py, float64 numpy) on the host cores: the reference
-itself is JAX/Pallas-TPU code that cannot run on this machine.
+``--impl reference`` times the fp32 C++/OpenMP restatement of the reference
+algorithm (oracle/gdn2_cpu.cpp, checked against the float64 oracle) on all
+host cores: the reference itself is JAX/Pallas-TPU code that cannot run on
+this machine.
 """
 from __future__ import annotations
 
@@ -201,69 +202,71 @@ def tensor_peak(cfg, bf16_tflops):
     return 148 * 128 * 2 * 1.965e9 / 1e12, "fp32 CUDA-core FMA (148 SMs x 128 x 2 x 1.965 GHz)"
 
 
-def _cpu_sample_worker(args):
-    """One (batch, head) slice of length T_s of config ``n`` through the
-    oracle (fwd+bwd, or fwd for a forward-only config); returns (tokens,
-    seconds of compute)."""
-    T_s, seed, n = args
-    cfg = CONFIGS[n]
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import gdn2_oracle as O
+def _cpu_inputs(cfg, slices, seed=100):
     from gdn2_package.synthetic import make_inputs
-    inp = make_inputs(1, T_s, 1, cfg["D"], seed=seed, h0_std=cfg["h0"], grads=cfg["bwd"])
-    a = [inp[n_] for n_ in ("q", "k", "v", "w", "b", "g")]
-    h0 = inp.get("h0")
+    return make_inputs(1, cfg["T"], slices, cfg["D"], seed=seed, h0_std=cfg["h0"],
+                       grads=cfg["bwd"])
+
+
+def _cpu_run(cfg, inp, threads):
+    """One fwd(+bwd) of the fp32 C++/OpenMP restatement of the reference
+    (oracle/gdn2_cpu.cpp) over the sample; returns seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import gdn2_cpu
     t0 = time.perf_counter()
-    O.forward(*a, inp["scale"], h0, cfg["BT"], cfg["BC"], cfg["CLIP"])
-    if cfg["bwd"]:
-        O.backward(*a, inp["scale"], h0, inp["dout"], inp["dh_final"], cfg["BT"], cfg["BC"],
-                   cfg["CLIP"])
-    return T_s, time.perf_counter() - t0
+    gdn2_cpu.fwd_bwd(inp, cfg["BT"], cfg["BC"], cfg["CLIP"], threads=threads, backward=cfg["bwd"])
+    return time.perf_counter() - t0
 
 
-def _single_thread_env():
-    for v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
-        os.environ[v] = "1"
+def _cpu_plan(cfg):
+    """(slices, threads): one (batch, head) slice per host core, at most the
+    configuration's B*H, each at the full T."""
+    cores = os.cpu_count() or 1
+    return min(cfg["B"] * cfg["H"], cores), cores
+
+
+def _cpu_sample_text(cfg, slices, threads, dt=None):
+    mode = "fwd+bwd" if cfg["bwd"] else "fwd"
+    t = f" ({dt:.1f} s)" if dt is not None else ""
+    return (f"{slices} of the {cfg['B'] * cfg['H']} (batch, head) slices of the workload at the "
+            f"full T={cfg['T']}, {mode} (the forward recomputed in the backward, as the reference "
+            f"does), fp32 C++/OpenMP restatement of the reference on {threads} threads{t}; "
+            f"tokens = slices x T")
 
 
 def run_reference(args, rank, world):
-    """The reference's algorithm on the host cores: every core runs one
-    (batch, head) slice of the configuration at its full length T through the
-    float64 numpy oracle; throughput = tokens of all slices / the slowest
-    slice's compute time (one slice is 1/(B*H) of the job)."""
+    """The reference's algorithm on the host cores: the fp32 C++/OpenMP
+    restatement (oracle/gdn2_cpu.cpp) over one (batch, head) slice per core at
+    the configuration's full length T; throughput = tokens of the sample /
+    its wall time.  The reference itself is JAX/Pallas for TPU and cannot run
+    here."""
     if rank != 0:
         return
-    import multiprocessing as mp
-    _single_thread_env()
     cfg = CONFIGS[args.config]
-    procs = os.cpu_count() or 1
-    T_s = cfg["T"]
+    slices, threads = _cpu_plan(cfg)
+    inp = _cpu_inputs(cfg, slices)
     vals, wall = [], 0.0
-    with mp.get_context("spawn").Pool(procs) as pool:
-        for i in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            res = pool.map(_cpu_sample_worker, [(T_s, 100 + j, args.config) for j in range(procs)])
-            dt = time.perf_counter() - t0
-            if i >= args.warmup:
-                vals.append(sum(r[0] for r in res) / max(r[1] for r in res))
-                wall += dt
+    for i in range(args.warmup + args.steps):
+        dt = _cpu_run(cfg, inp, threads)
+        if i >= args.warmup:
+            vals.append(slices * cfg["T"] / dt)
+            wall += dt
     value = statistics.median(vals)
-    mode = "fwd+bwd" if cfg["bwd"] else "fwd"
-    sample = (f"each step: {procs} processes, each one (batch, head) slice of the workload at "
-              f"its full T={T_s} (float64 numpy oracle, {mode}); tokens / slowest slice's time")
+    sample = _cpu_sample_text(cfg, slices, threads)
     line = {
         "impl": "reference", "metric": METRIC if args.config == 1 else metric_of(cfg),
         "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(args.steps, 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (reference distributions, seeded)",
         "config": {"workload": workload_of(cfg, args.config), "sample": sample,
                    "same_config": True},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is JAX/Pallas-TPU code and JAX is not installed here; the timed "
-                "arm is the CPU restatement of its algorithm",
+                "arm is an fp32 C++/OpenMP restatement of its algorithm, checked against the "
+                "float64 oracle pinned to the reference's own outputs",
     }
     print(json.dumps(line), flush=True)
 
@@ -428,12 +431,11 @@ def run_ours(args, rank, world, local_rank):
                          "against the same peaks")
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        _single_thread_env()
-        T_s = T if cfg["bwd"] else min(T, 2048)
-        tok, dt = _cpu_sample_worker((T_s, 1, args.config))
-        cpu = {"value": tok / dt, "unit": UNIT, "cores": 1, "kind": "port",
-               "sample": f"one (batch, head) slice of the workload, T={T_s}, through the float64 "
-                         f"numpy oracle on one core ({dt:.1f} s)"}
+        slices, threads = _cpu_plan(cfg)
+        cinp = _cpu_inputs(cfg, slices)
+        dt = _cpu_run(cfg, cinp, threads)
+        cpu = {"value": slices * T / dt, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": _cpu_sample_text(cfg, slices, threads, dt)}
     line = {
         "metric": METRIC if args.config == 1 else metric_of(cfg),
         "value": tokens / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
