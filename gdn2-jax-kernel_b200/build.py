@@ -43,7 +43,9 @@ def build(force=False, verbose=False):
     procs = []
     for src in SOURCES:
         obj = os.path.join(bdir, src.replace(".cu", ".o"))
-        cmd = [_nvcc(), *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        # GDN2_NVCC_EXTRA: extra flags, e.g. -DGDN2_PHASE_TIMING for the
+        # per-phase cycle counts of the tensor-core kernels
+        cmd = [_nvcc(), *NVCC_FLAGS, *os.environ.get("GDN2_NVCC_EXTRA", "").split(), "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         procs.append((cmd, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)))

@@ -238,6 +238,22 @@ int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* s
          (host[4] ? GDN2_STATUS_B4_EXACT : 0);
 }
 
+int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, size_t head_bytes,
+                    int to_device, void* stream) {
+  if (!host || !dev || rows < 0 || H <= 0 || Hs <= 0 || h0 < 0 || h0 + Hs > H || head_bytes == 0)
+    return fail(GDN2_ERR_INVALID, "%sgdn2_copy_heads: bad pointers or head range");
+  if (rows == 0) return GDN2_OK;
+  char* hp = static_cast<char*>(host) + (size_t)h0 * head_bytes;
+  const size_t hpitch = (size_t)H * head_bytes, dpitch = (size_t)Hs * head_bytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      to_device ? cudaMemcpy2DAsync(dev, dpitch, hp, hpitch, dpitch, (size_t)rows,
+                                    cudaMemcpyHostToDevice, s)
+                : cudaMemcpy2DAsync(hp, hpitch, dev, dpitch, dpitch, (size_t)rows,
+                                    cudaMemcpyDeviceToHost, s);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_copy_heads");
+}
+
 int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }
 
 int gdn2_profile_enable(int on) {

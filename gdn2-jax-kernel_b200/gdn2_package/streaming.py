@@ -8,10 +8,10 @@ layer in a single call.
 
 With CUDA tensors it runs the forward (keeping its per-chunk residuals) and
 the backward on the current stream.  With host tensors, every (batch, head)
-being independent (gdn2_fwd.py:154), the batch is cut into shards that flow
-through a ring of device buffer sets on three streams: the copy of shard s+1
-to the device, the kernels of shard s and the copy of shard s-1 back to the
-host overlap, so the step costs about the larger of the PCIe traffic and the
+being independent (gdn2_fwd.py:154), the batch is cut into (batch rows x
+head group) shards that flow through a ring of device buffer sets: the copy of shard s+1 to the device
+(one stream), the kernels of the shards in flight (one stream per buffer
+set) and the copy of shard s-1 back to the host (one stream) overlap, so the step costs about the larger of the PCIe traffic and the
 compute instead of their sum.  Results equal the unsharded call (the same
 kernels run on every (batch, head)).
 """
@@ -64,12 +64,24 @@ def _run(p, lib, code, xs, h0, do, dhf, o, hf, grads, dh0, ws, Bs, stream):
     _lib.check(rc, "gdn2_bwd")
 
 
+def _head_group(Bs, T, H, D=128):
+    """Smallest head group whose shard still gives the chunk kernels one CTA
+    per SM (148 on a B200): small shards shorten the copy-in of the first
+    shard and the copy-out of the last, which nothing overlaps."""
+    nc = max(1, T // _fwd._kernel_chunk(T, int(_fwd.BT), D))
+    for hs in range(1, H + 1):
+        if H % hs == 0 and Bs * hs * nc >= 148:
+            return hs
+    return H
+
+
 def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, shard=1, depth=3,
-                 out=None):
+                 out=None, heads=None):
     """Forward and backward of one layer call (forward only when ``dout`` is
     None; a missing ``dh_final`` is zero).  Host tensors (pinned for
-    asynchronous copies) are streamed in batch shards of ``shard`` rows with
-    ``depth`` shards in flight; ``out`` may hold preallocated host outputs
+    asynchronous copies) are streamed in shards of ``shard`` batch rows by
+    ``heads`` heads (default: the smallest group that fills the GPU), each
+    tensor moved by one pitched copy, with ``depth`` shards in flight; ``out`` may hold preallocated host outputs
     ``(o, h_final[, dq, dk, dv, dw, db, dg, dh0])``.  Gradients come back in
     the input dtype, o / h_final / dh0 in float32; the gradient tuple is None
     for a forward only."""
@@ -98,18 +110,22 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
         raise _fwd.Gdn2ShapeError("streamed inputs must share one dtype, float32 or bfloat16")
     if T % int(_fwd.BT):
         raise _fwd.Gdn2ShapeError(f"L={T} must be divisible by BT={_fwd.BT}.")
+    do_h = dhf_h = None
     if bwd:
         do_h = torch.as_tensor(dout).float().contiguous()
-        dhf_h = torch.zeros((B, H, D, D)) if dh_final is None else \
-            torch.as_tensor(dh_final).float().contiguous()
+        if dh_final is not None:
+            dhf_h = torch.as_tensor(dh_final).float().contiguous()
     h0_h = None if h0 is None else torch.as_tensor(h0).float().contiguous()
     Bs = max(1, min(int(shard), B))
     if B % Bs:
         raise _fwd.Gdn2ShapeError(f"shard={Bs} must divide the batch B={B}")
+    Hs = _head_group(Bs, T, H, D) if heads is None else max(1, min(int(heads), H))
+    if H % Hs:
+        raise _fwd.Gdn2ShapeError(f"heads={Hs} must divide the head count H={H}")
     dev = torch.device("cuda", torch.cuda.current_device())
     # constants and chunking are validated exactly as for the device path
-    p = _fwd._Prepared(*[torch.empty((Bs, T, H, D), dtype=dt, device=dev)] * 6, scale,
-                       None if h0_h is None else torch.empty((Bs, H, D, D), device=dev))
+    p = _fwd._Prepared(*[torch.empty((Bs, T, Hs, D), dtype=dt, device=dev)] * 6, scale,
+                       None if h0_h is None else torch.empty((Bs, Hs, D, D), device=dev))
     lib = _lib.load()
     if out is None:
         pin = torch.cuda.is_available()
@@ -117,31 +133,52 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
         out = (mk((B, T, H, D), torch.float32), mk((B, H, D, D), torch.float32))
         if bwd:
             out += (*[mk((B, T, H, D), dt) for _ in NAMES], mk((B, H, D, D), torch.float32))
+    if any(not t.is_contiguous() for t in out):
+        raise _fwd.Gdn2ShapeError("preallocated host outputs must be contiguous")
     o_h, hf_h, *g_h = out
     dh0_h = g_h.pop() if bwd else None
-    nsh = B // Bs
+    nb, nhg = B // Bs, H // Hs
+    nsh = nb * nhg
     nslot = max(1, min(int(depth), nsh))
     slots = [_Slot(p, Bs, dev, h0_h is not None, bwd) for _ in range(nslot)]
     # each shard's status header (gdn2_workspace_status) lands in pinned memory
     status_h = torch.zeros((nsh, 5), dtype=torch.int32, pin_memory=True)
-    s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    # one compute stream per slot: the kernels of consecutive shards overlap,
+    # which hides the latency of the chunk scans (sequential over a shard's
+    # chunks, so a small shard leaves most SMs idle while they run)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_runs = [torch.cuda.Stream(dev) for _ in range(nslot)]
     cur = torch.cuda.current_stream(dev)
-    for st in (s_in, s_run, s_out):
+    for st in (s_in, s_out, *s_runs):
         st.wait_stream(cur)
+
+    def copy(host, devt, b0, h0, seq, to_device, stream):
+        # one pitched DMA per tensor: rows (b, t) of the shard, heads h0 .. h0+Hs-1
+        eb = host.element_size()
+        head = (D if seq else D * D) * eb
+        rows = Bs * (T if seq else 1)
+        hp = host.data_ptr() + b0 * (T if seq else 1) * H * head
+        _lib.check(lib.gdn2_copy_heads(hp, devt.data_ptr(), rows, H, h0, Hs, head, int(to_device),
+                                       stream.cuda_stream), "gdn2_copy_heads")
+
     for s in range(nsh):
         sl = slots[s % nslot]
-        rows = slice(s * Bs, (s + 1) * Bs)
-        with torch.cuda.stream(s_in):
-            if s >= nslot:
-                s_in.wait_event(sl.computed)        # the kernels of shard s - nslot read these
-            for dst, src in zip(sl.x, xs):
-                dst.copy_(src[rows], non_blocking=True)
-            if bwd:
-                sl.do.copy_(do_h[rows], non_blocking=True)
-                sl.dhf.copy_(dhf_h[rows], non_blocking=True)
-            if sl.h0 is not None:
-                sl.h0.copy_(h0_h[rows], non_blocking=True)
-            sl.loaded.record(s_in)
+        b0, h0s = (s // nhg) * Bs, (s % nhg) * Hs
+        if s >= nslot:
+            s_in.wait_event(sl.computed)        # the kernels of shard s - nslot read these
+        for dst, src in zip(sl.x, xs):
+            copy(src, dst, b0, h0s, True, True, s_in)
+        if bwd:
+            copy(do_h, sl.do, b0, h0s, True, True, s_in)
+            if dhf_h is None:
+                with torch.cuda.stream(s_in):
+                    sl.dhf.zero_()
+            else:
+                copy(dhf_h, sl.dhf, b0, h0s, False, True, s_in)
+        if sl.h0 is not None:
+            copy(h0_h, sl.h0, b0, h0s, False, True, s_in)
+        sl.loaded.record(s_in)
+        s_run = s_runs[s % nslot]
         s_run.wait_event(sl.loaded)
         if s >= nslot:
             s_run.wait_event(sl.drained)            # outputs of shard s - nslot copied out
@@ -152,16 +189,16 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
             status_h[s].copy_(sl.ws[off:off + 20].view(torch.int32), non_blocking=True)
         sl.computed.record(s_run)
         s_out.wait_event(sl.computed)
-        with torch.cuda.stream(s_out):
-            o_h[rows].copy_(sl.o, non_blocking=True)
-            hf_h[rows].copy_(sl.hf, non_blocking=True)
-            for dst, src in zip(g_h, sl.g):
-                dst[rows].copy_(src, non_blocking=True)
-            if bwd:
-                dh0_h[rows].copy_(sl.dh0, non_blocking=True)
-            sl.drained.record(s_out)
+        copy(o_h, sl.o, b0, h0s, True, False, s_out)
+        copy(hf_h, sl.hf, b0, h0s, False, False, s_out)
+        for dst, src in zip(g_h, sl.g):
+            copy(dst, src, b0, h0s, True, False, s_out)
+        if bwd:
+            copy(dh0_h, sl.dh0, b0, h0s, False, False, s_out)
+        sl.drained.record(s_out)
     s_out.synchronize()
-    s_run.synchronize()
+    for st in s_runs:
+        st.synchronize()
     st = status_h.any(dim=0).tolist()
     _lib.LAST_STATUS = sum(bit for bit, on in zip(
         (_lib.STATUS_WAIT_TIMEOUT, _lib.STATUS_FWD_STATE_CLIPPED, _lib.STATUS_BWD_STATE_CLIPPED,

@@ -149,6 +149,17 @@ int gdn2_fwd_noalloc(int dtype, const void* q, const void* k, const void* v, con
  * the status of the latest gdn2_fwd_noalloc call there (synchronizes `stream`). */
 int gdn2_noalloc_status(void* stream);
 
+/* Copies one head group of a host batch shard to or from the device with a
+ * single pitched DMA (the streamed host path, gdn2_fwd_bwd in the Python
+ * package).  `host` points at row 0 of the shard in the caller's layout
+ * [rows][H][head_bytes] (e.g. rows = batch rows x T for (B,T,H,D) tensors,
+ * head_bytes = D x element size; rows = batch rows, head_bytes = D x D x 4
+ * for (B,H,D,D) states); `dev` is the packed [rows][Hs][head_bytes] device
+ * buffer of heads h0 .. h0+Hs-1.  to_device = 1 copies host -> dev, 0 copies
+ * dev -> host.  Asynchronous on `stream` (pinned host memory for overlap). */
+int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, size_t head_bytes,
+                    int to_device, void* stream);
+
 /* Token-by-token decode of a short segment (B, T, H, D), carrying the state
  * h0 (B,H,D,D, may be NULL = zero) to h_final: the recurrence of
  * gdn2_pallas_forward (gdn2_fwd.py:338-362, state API gdn2_fwd.py:400-404)

@@ -94,6 +94,24 @@ def test_status_query_rejects_bad_workspace_without_gpu_work():
     assert lib.gdn2_selftest_wait_timeout(None, 1 << 20, 16, None) == _lib.ERR_INVALID
 
 
+def test_copy_heads_rejects_bad_ranges_without_gpu_work():
+    lib = _lib.load()
+    h, d = ctypes.c_void_p(4096), ctypes.c_void_p(8192)
+    assert lib.gdn2_copy_heads(None, d, 4, 6, 0, 3, 512, 1, None) == _lib.ERR_INVALID
+    assert lib.gdn2_copy_heads(h, d, 4, 6, 4, 3, 512, 1, None) == _lib.ERR_INVALID   # 4+3 > 6
+    assert lib.gdn2_copy_heads(h, d, 4, 6, 0, 0, 512, 0, None) == _lib.ERR_INVALID
+    assert lib.gdn2_copy_heads(h, d, 4, 6, 0, 2, 0, 0, None) == _lib.ERR_INVALID
+    assert lib.gdn2_copy_heads(h, d, 0, 6, 0, 2, 512, 0, None) == _lib.OK            # nothing to move
+
+
+def test_streamed_head_group_fills_the_gpu():
+    from gdn2_package.streaming import _head_group
+    assert _head_group(1, 8192, 6) == 3      # 64 chunks x 3 heads >= 148 CTAs
+    assert _head_group(1, 32768, 6) == 1
+    assert _head_group(2, 8192, 6) == 2
+    assert _head_group(1, 256, 4) == 4       # never fills: the whole head range
+
+
 def test_check_status_modes(monkeypatch):
     """The Python layer reads the status word only where its mode says, and a
     timed-out wait raises Gdn2Error (the read itself faked: no GPU here)."""

@@ -365,17 +365,19 @@ def test_config4_forward_with_state():
 
 @pytest.mark.parametrize("dtype,backward", [(torch.float32, True), (torch.bfloat16, True),
                                             (torch.float32, False)])
-def test_streamed_host_batches_equal_device_call(dtype, backward):
-    """gdn2_fwd_bwd on host tensors (batch shards streamed through a ring of
-    device buffers) gives the same bits as the device-resident call."""
+@pytest.mark.parametrize("shard,heads", [(1, 1), (1, 2), (5, 1), (1, None)])
+def test_streamed_host_batches_equal_device_call(dtype, backward, shard, heads):
+    """gdn2_fwd_bwd on host tensors ((batch rows x head group) shards moved
+    by pitched copies through a ring of device buffers) gives the same bits
+    as the device-resident call."""
     from gdn2_package import gdn2_fwd_bwd
     _set_consts(128, 64, 1e3)
-    inp = make_inputs(5, 256, 2, 128, seed=17, h0_std=0.1)
+    inp = make_inputs(5, 256, 4, 128, seed=17, h0_std=0.1)
     host = [torch.as_tensor(inp[n]).to(dtype).pin_memory() for n in NAMES]
     h0 = torch.as_tensor(inp["h0"])
     do = torch.as_tensor(inp["dout"]) if backward else None
     dhf = torch.as_tensor(inp["dh_final"]) if backward else None
-    o, h, g = gdn2_fwd_bwd(*host, inp["scale"], do, dhf, h0, shard=1, depth=2)
+    o, h, g = gdn2_fwd_bwd(*host, inp["scale"], do, dhf, h0, shard=shard, depth=2, heads=heads)
     assert o.device.type == "cpu"
     o2, h2, g2 = gdn2_fwd_bwd(*[t.cuda() for t in host], inp["scale"],
                               None if do is None else do.cuda(),
