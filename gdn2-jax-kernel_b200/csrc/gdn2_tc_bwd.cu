@@ -20,8 +20,23 @@
       printf("\n");                                                                 \
     }                                                                                \
   } while (0)
-#define GDN2_TDECL long long tmark[16]
+#define GDN2_TDECL long long tmark[16]; long long tsub[4] = {0, 0, 0, 0}, tsub0 = 0
+#define GDN2_TSUB(i)                                                                   \
+  do {                                                                                 \
+    if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) {                             \
+      const long long t_ = clock64();                                                  \
+      if (i > 0) tsub[i - 1] += t_ - tsub0;                                            \
+      tsub0 = t_;                                                                      \
+    }                                                                                  \
+  } while (0)
+#define GDN2_TSUBPRINT(name)                                                           \
+  do {                                                                                 \
+    if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)                               \
+      printf("%s slices: %lld %lld %lld %lld\n", name, tsub[0], tsub[1], tsub[2], tsub[3]); \
+  } while (0)
 #else
+#define GDN2_TSUB(i) do { } while (0)
+#define GDN2_TSUBPRINT(name) do { } while (0)
 #define GDN2_TMARK(i) do { } while (0)
 #define GDN2_TPRINT(name, n) do { } while (0)
 #define GDN2_TDECL
@@ -539,42 +554,85 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       if (pass > 0) GDN2_TMARK(1 + 2 * pass);
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
       const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
+      // Every global load of a slice is issued first (one memory latency per
+      // slice), and the MMAs of slice sl are issued during slice sl+1 while
+      // its loads are in flight: the issuing thread blocks for about as long
+      // as the tensor core takes, and that wait overlaps the load latency
+      // instead of delaying its warp's staging.  (Loading slice sl+1 during
+      // slice sl needs registers the dk / dgc accumulators hold.)
+      const int e = threadIdx.x;
+      const int rb = (e & 7) + ((e >> 5) & 3) * 8, kb = ((e >> 3) & 3) + (e >> 7) * 4;
+      const int d0 = rb * 4;   // this thread's 4 x 4 block of the second operand
+      auto load_slice = [&](int k0, Frag& fm, Frag& fx) {
+        if (left) {
+          load_trans(fm, MT, C, k0);                      // (i, jj) = dM(i, k0+jj)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) fx.v[j] = ld4<T>(kc + (k0 + kb * 4 + j) * rs + d0);
+        } else {
+          load_direct(fm, MT, C, k0);                     // (j, ii) = dM(k0+ii, j)
+          const T* src = pass == 2 ? qc : kc;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) fx.v[j] = ld4<T>(src + (k0 + kb * 4 + j) * rs + d0);
+        }
+      };
+      Frag fm, fx;
+      int pend_buf = -1, pend_J = 0;
+      bool pend_acc = false;
 #pragma unroll 1
       for (int sl = 0; sl < 4; ++sl, ++gs) {
         const int J = sl * 32 / JW, r = JW * J, k0 = 32 * sl;   // K slice k0 of block J
         const int buf = gs & 1;
+        GDN2_TSUB(0);
         ring_acquire(ring, buf, gs >> 1, ws.status);
+        GDN2_TSUB(1);
+        load_slice(k0, fm, fx);
+        Frag fb;   // the gate of pass 3
+        if (pass == 3) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            fb.v[j] = ld4_gate<T>(bc + (k0 + kb * 4 + j) * rs + d0, GATES, kGateB);
+        }
+        if (threadIdx.x == 0 && pend_buf >= 0) {
+          mma3(tmem + 128 * pend_J, ring.op(pend_buf, 0), ring.op(pend_buf, 1), 128, KS / 8, pend_acc);
+          commit(&ring.bars[pend_buf]);
+        }
+        const float4 gr = ldg4(gc + r * GLD + d0);
         if (left) {
-          stage_trans(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, k0, Ident{});   // (i, jj) = dM(i, k0+jj)
-          stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, jj) = R
-            const int j = k0 + kk;
-            const float4 kv = ld4<T>(kc + j * rs + d);
-            const float4 gj = ldg4(gc + j * GLD + d), gr = ldg4(gc + r * GLD + d);
-            return make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
-                               kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w));
-          });
+          store_trans(ring.hi(buf, 0), ring.lo(buf, 0), fm);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {   // (d, jj) = R = k_j e^{gc_r - gc_j}
+            const float4 gj = ldg4(gc + (k0 + kb * 4 + j) * GLD + d0);
+            const float4 kv = fx.v[j];
+            fx.v[j] = make_float4(kv.x * __expf(gr.x - gj.x), kv.y * __expf(gr.y - gj.y),
+                                  kv.z * __expf(gr.z - gj.z), kv.w * __expf(gr.w - gj.w));
+          }
         } else {
-          stage_direct(ring.hi(buf, 0), ring.lo(buf, 0), MT, C, k0, Ident{});  // (j, ii) = dM(k0+ii, j)
-          stage_trans_f(ring.hi(buf, 1), ring.lo(buf, 1), [&](int kk, int d) {   // (d, ii) = L
-            const int i = k0 + kk;
-            const float4 gi = ldg4(gc + i * GLD + d), gr = ldg4(gc + r * GLD + d);
-            float4 lv;
+          store_direct(ring.hi(buf, 0), ring.lo(buf, 0), fm);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {   // (d, ii) = L = l_i e^{gc_i - gc_r}
+            const float4 gi = ldg4(gc + (k0 + kb * 4 + j) * GLD + d0);
+            float4 lv = fx.v[j];
             if (pass == 2) {
-              const float4 qv = ld4<T>(qc + i * rs + d);
-              lv = make_float4(p.scale * qv.x, p.scale * qv.y, p.scale * qv.z, p.scale * qv.w);
+              lv = scl(lv, p.scale);
             } else {
-              const float4 kv = ld4<T>(kc + i * rs + d), bv = ld4_gate<T>(bc + i * rs + d, GATES, kGateB);
-              lv = make_float4(bv.x * kv.x, bv.y * kv.y, bv.z * kv.z, bv.w * kv.w);
+              const float4 bv = fb.v[j];
+              lv = make_float4(bv.x * lv.x, bv.y * lv.y, bv.z * lv.z, bv.w * lv.w);
             }
-            return make_float4(lv.x * __expf(gi.x - gr.x), lv.y * __expf(gi.y - gr.y),
-                               lv.z * __expf(gi.z - gr.z), lv.w * __expf(gi.w - gr.w));
-          });
+            fx.v[j] = make_float4(lv.x * __expf(gi.x - gr.x), lv.y * __expf(gi.y - gr.y),
+                                  lv.z * __expf(gi.z - gr.z), lv.w * __expf(gi.w - gr.w));
+          }
         }
+        store_trans(ring.hi(buf, 1), ring.lo(buf, 1), fx);
+        GDN2_TSUB(2);
         slice_publish();
-        if (threadIdx.x == 0) {
-          mma3(tmem + 128 * J, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, k0 > r);
-          commit(&ring.bars[buf]);
-        }
+        GDN2_TSUB(3);
+        pend_buf = buf;
+        pend_J = J;
+        pend_acc = k0 > r;
+      }
+      if (threadIdx.x == 0) {
+        mma3(tmem + 128 * pend_J, ring.op(pend_buf, 0), ring.op(pend_buf, 1), 128, KS / 8, pend_acc);
+        commit(&ring.bars[pend_buf]);
       }
       drain(&ts.done, ph, ws.status);
       GDN2_TMARK(2 + 2 * pass);
@@ -739,6 +797,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   teardown(tmem);
   GDN2_TMARK(11);
   GDN2_TPRINT("bwd_intra3", 12);
+  GDN2_TSUBPRINT("bwd_intra3");
 }
 
 template <typename T>
