@@ -27,6 +27,7 @@ struct Profiler {
 Profiler g_prof;
 std::mutex g_prof_mu;
 int g_diag = 0;   // per-stage diagnostics on (gdn2_diag_enable)
+int g_pair64 = 0;  // BT = 64 chunks paired into 128-row tensor-core tiles (gdn2_pair64_enable)
 
 void prof_hook(int stage, int end, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -160,6 +161,10 @@ int run_bwd_intra(int BT, int D, const void* q, const void* k, const void* v, co
 // Chunk = head dim = 128 runs the inter-chunk recurrence on the tensor cores
 // (affine scan, gdn2_tc_kernels.cu); other shapes use the CUDA-core kernels.
 bool use_tc(int BT, int D) { return BT == 128 && D == 128; }
+// BT = 64 with D = 128 runs on the tensor-core kernels with two chunks per
+// 128-row tile (block-diagonal scores and solve, per-chunk gates, a state
+// step per chunk) when T is a multiple of 128.
+bool use_pair64(int T, int D, int BT) { return g_pair64 && BT == 64 && D == 128 && T % 128 == 0; }
 
 // Every entry point clears the status header of its workspace first, so the
 // word gdn2_workspace_status() reads belongs to the latest call.
@@ -173,6 +178,7 @@ Problem make_problem(int B, int T, int H, int D, int BT, int BC, float scale, fl
   p.B = B; p.T = T; p.H = H; p.D = D; p.C = BT; p.nc = T / BT; p.bc = BC;
   p.diag = g_diag;
   p.gates = 0;
+  p.sub = 1;
   p.scale = scale; p.clip = clip;
   return p;
 }
@@ -200,6 +206,12 @@ extern "C" {
 int gdn2_diag_enable(int on) {
   g_diag = on != 0;
   return GDN2_OK;
+}
+
+int gdn2_pair64_enable(int on) {
+  const int prev = g_pair64;
+  g_pair64 = on != 0;
+  return prev;
 }
 
 int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
@@ -287,7 +299,14 @@ const char* gdn2_last_error(void) { return g_err; }
 
 size_t gdn2_workspace_bytes(int B, int T, int H, int D, int BT, int with_backward) {
   if (B <= 0 || T <= 0 || H <= 0 || D <= 0 || BT <= 0 || T % BT) return 0;
-  return Workspace::required_bytes(B, H, T / BT, BT, D, with_backward != 0);
+  size_t n = Workspace::required_bytes(B, H, T / BT, BT, D, with_backward != 0);
+  // BT = 64, D = 128: enough for either kernel family, so the answer does
+  // not depend on gdn2_pair64_enable
+  if (BT == 64 && D == 128 && T % 128 == 0) {
+    const size_t m = Workspace::required_bytes(B, H, T / 128, 128, D, with_backward != 0, 2);
+    if (m > n) n = m;
+  }
+  return n;
 }
 
 int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void* w,
@@ -302,17 +321,20 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  const bool pair = use_pair64(T, D, BT) && !save_residuals;   // TODO backward
+  const int KT = pair ? 128 : BT;   // kernel tile rows
+  Problem p = make_problem(B, T, H, D, KT, BC, scale, clip);
+  p.sub = pair ? 2 : 1;
   p.gates = (dtype & GDN2_GATES_RAW) != 0;
   dtype &= ~GDN2_GATES_RAW;
-  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, false);
+  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, KT, D, false, p.sub);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;
   rc = dtype == GDN2_F32
-           ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
-           : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
+           ? run_fwd_intra<float>(KT, D, q, k, v, w, b, g, p, ws, s)
+           : run_fwd_intra<__nv_bfloat16>(KT, D, q, k, v, w, b, g, p, ws, s);
   if (rc) return rc;
-  if (use_tc(BT, D)) {
+  if (use_tc(KT, D)) {
     cudaError_t e = launch_tc_fwd(p, ws, h0, o, h_final, s, hook());
     return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "tc_fwd");
   }

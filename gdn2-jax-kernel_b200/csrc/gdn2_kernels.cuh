@@ -188,8 +188,10 @@ __device__ __forceinline__ void wy_inverse_T(float* S, int ld, float* tmp, int b
 
 // Column-wise inclusive prefix sum of a C x D tile held row-major in shared
 // memory (ld = D).  256 threads: each column split into 256/D row segments.
+// restart = true: each RS-row segment is summed on its own (two 64-row
+// chunks per 128-row tile).
 template <int C, int D, int LD = D>
-__device__ __forceinline__ void column_cumsum(float* s, float* tot) {
+__device__ __forceinline__ void column_cumsum(float* s, float* tot, bool restart = false) {
   constexpr int NSEG = kThreads / D;
   constexpr int RS = C / NSEG;
   const int d = threadIdx.x % D, seg = threadIdx.x / D;
@@ -199,7 +201,8 @@ __device__ __forceinline__ void column_cumsum(float* s, float* tot) {
   tot[seg * D + d] = acc;
   __syncthreads();
   float off = 0.f;
-  for (int sg = 0; sg < seg; ++sg) off += tot[sg * D + d];
+  if (!restart)
+    for (int sg = 0; sg < seg; ++sg) off += tot[sg * D + d];
 #pragma unroll 8
   for (int r = seg * RS; r < (seg + 1) * RS; ++r) {
     off += s[r * LD + d];
@@ -271,8 +274,10 @@ __device__ __forceinline__ void wy_level_tiled(float* S, int ld, float* tmp, flo
 // A10 = san(-A11 tmp) on register tiles; for BC = 32 the 16-row step inside a
 // sub-block is one register-tiled level.  Other BC take the generic
 // substitution.  `tmp` needs 4096 floats, `scr` 2 * 64 * 68.
+// `span` = rows of one reference chunk: 128, or 64 when the tile holds two
+// chunks (block-diagonal T; the two 64-row groups are solved independently).
 __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, float* scr, int bc,
-                                                float clip) {
+                                                float clip, int span = 128) {
   constexpr int C = 128, H = 64, LY = 68;
 #ifdef GDN2_PHASE_TIMING
   long long t0 = clock64();
@@ -289,8 +294,8 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
   long long t2 = clock64();
   if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0) wy_t[0] = t1 - t0, wy_t[1] = t2 - t1;
 #endif
-  if (bc != 64) {
-    if (C > bc) wy_compose_blocks(S, ld, C, bc, C / bc, tmp, clip);
+  if (bc != 64 || span != C) {
+    if (span > bc) wy_compose_blocks(S, ld, C, bc, span / bc, tmp, clip);
     return;
   }
   // last level: T10 = M(64.., 0..63), A00 = A(0..63, 0..63), A11 = A(64.., 64..)
@@ -333,7 +338,7 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
 // Reverse (suffix) column sum of a C x D tile in shared memory (ld = D),
 // the in-chunk reverse cumsum of gdn2_bwd.py:32-41.  `tot` >= 256 floats.
 template <int C, int D>
-__device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
+__device__ __forceinline__ void column_revcumsum(float* s, float* tot, bool restart = false) {
   constexpr int NSEG = kThreads / D;
   constexpr int RS = C / NSEG;
   const int d = threadIdx.x % D, seg = threadIdx.x / D;
@@ -342,7 +347,8 @@ __device__ __forceinline__ void column_revcumsum(float* s, float* tot) {
   tot[seg * D + d] = acc;
   __syncthreads();
   float off = 0.f;
-  for (int sg = seg + 1; sg < NSEG; ++sg) off += tot[sg * D + d];
+  if (!restart)
+    for (int sg = seg + 1; sg < NSEG; ++sg) off += tot[sg * D + d];
   for (int r = (seg + 1) * RS - 1; r >= seg * RS; --r) {
     off += s[r * D + d];
     s[r * D + d] = off;

@@ -127,7 +127,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   for (int e = threadIdx.x; e < C * D; e += kThreads) gpos = fmaxf(gpos, sgc[(e / D) * GLD + e % D]);
   const float gmax = block_max(gpos, red);
   GDN2_TMARK(9);
-  column_cumsum<C, D, GLD>(sgc, red);
+  // chunk-local gc: with two 64-row chunks per tile the cumsum restarts at row 64
+  column_cumsum<C, D, GLD>(sgc, red, p.sub == 2);
+  const int R = C / p.sub;   // rows of one reference chunk
   GDN2_TMARK(10);
   // largest decay-block width (64 or 32 rows) whose in-block gc spread keeps
   // every factor e^{gc_r - gc_j} inside the float range
@@ -145,9 +147,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     for (int e = threadIdx.x * 4; e < C * D; e += kThreads * 4)
       sts4(gco + e, lds4(sgc + (e / D) * GLD + e % D));
     GDN2_TMARK(12);
-    if (threadIdx.x < D) ws.gcl[chunk * D + threadIdx.x] = san(sgc[(C - 1) * GLD + threadIdx.x], p.clip);
+    for (int e = threadIdx.x; e < p.sub * D; e += kThreads)
+      ws.gcl[chunk * p.sub * D + e] = san(sgc[((e / D) * R + R - 1) * GLD + e % D], p.clip);
     float* kgo = ws.kg + chunk * C * D;
-    const float* gl = sgc + (C - 1) * GLD;
     // qg is staged transposed with an odd row stride; a warp covers 4 rows x 32
     // columns, so the transposed scalar stores hit 32 distinct banks and the
     // global rows are read in 128-byte pieces.
@@ -162,7 +164,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       int i, d;
       kq_at(4 * bt + u, i, d);
       const float4 kv = kcur[u], qv = qcur[u];
-      const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(gl + d);
+      const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(sgc + ((i / R) * R + R - 1) * GLD + d);
       const float4 kg4 = make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
                                      san(kv.y * __expf(l4.y - gi.y), p.clip),
                                      san(kv.z * __expf(l4.z - gi.z), p.clip),
@@ -203,8 +205,11 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       dqg.flush(ws.status, kDiagQg);
     }
     // max_i ||kg_i||_1, the gain of dv_new's kg dh term (backward guard)
-    const float kl1 = block_max(threadIdx.x < C ? ts.rowl1[threadIdx.x] : 0.f, red);
-    if (threadIdx.x == 0) ws.bnd[chunk * 4] = kl1;
+    for (int hf = 0; hf < p.sub; ++hf) {
+      const bool mine = threadIdx.x >= hf * R && threadIdx.x < (hf + 1) * R;
+      const float kl1 = block_max(mine ? ts.rowl1[threadIdx.x] : 0.f, red);
+      if (threadIdx.x == 0) ws.bnd[(chunk * p.sub + hf) * 4] = kl1;
+    }
   }
 
   GDN2_TMARK(1);
@@ -265,7 +270,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           rc_of(it, i, cc);
           const int d = s * KS + cc;
           float4 aq = make_float4(0.f, 0.f, 0.f, 0.f), ak = aq;
-          if (i >= r) {
+          // rows of the column block's own chunk only (block-diagonal when
+          // the tile holds two chunks)
+          if (i >= r && i / R == r / R) {
             const float4 gi = lds4(sgc + i * GLD + d), gr = lds4(sgc + r * GLD + d);
             const float e0 = __expf(gi.x - gr.x), e1 = __expf(gi.y - gr.y),
                         e2 = __expf(gi.z - gr.z), e3 = __expf(gi.w - gr.w);
@@ -303,7 +310,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {   // Aqk / scale
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        aqkT[(c + t) * C + i] = c + t <= i ? san(p.scale * v[t], p.clip) : 0.f;
+        aqkT[(c + t) * C + i] = c + t <= i && (c + t) / R == i / R ? san(p.scale * v[t], p.clip) : 0.f;
         if (DIAG) dsc.add(aqkT[(c + t) * C + i]);
       }
     });
@@ -311,7 +318,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // S[j][i] = Akk(i, j)
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        S[(c + t) * TLD + i] = c + t < i ? san(v[t], p.clip) : 0.f;
+        S[(c + t) * TLD + i] = c + t < i && (c + t) / R == i / R ? san(v[t], p.clip) : 0.f;
         if (DIAG) dsc.add(S[(c + t) * TLD + i]);
       }
     });
@@ -320,8 +327,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     // exact elementwise form with the +-20 exponent clip (gdn2_fwd.py:124-139)
     for (int e = threadIdx.x; e < C * C; e += kThreads) {
       const int i = e % C, j = e / C;
+      const bool pair = j <= i && j / R == i / R;   // same chunk, causal
       float sq = 0.f, sk = 0.f;
-      if (j <= i) {
+      if (pair) {
         for (int d = 0; d < D; ++d) {
           const float ed = __expf(fminf(fmaxf(sgc[i * GLD + d] - sgc[j * GLD + d], -20.f), 20.f));
           const float kj = to_f<T>(kc[j * rs + d]) * ed;
@@ -329,8 +337,8 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           sk = fmaf(ld_gate<T>(bc + i * rs + d, GATES, kGateB) * to_f<T>(kc[i * rs + d]), kj, sk);
         }
       }
-      aqkT[j * C + i] = (j <= i) ? san(p.scale * sq, p.clip) : 0.f;
-      S[j * TLD + i] = (j < i) ? san(sk, p.clip) : 0.f;
+      aqkT[j * C + i] = pair ? san(p.scale * sq, p.clip) : 0.f;
+      S[j * TLD + i] = (pair && j < i) ? san(sk, p.clip) : 0.f;
       if (DIAG) {
         dsc.add(aqkT[j * C + i]);
         dqg.add(S[j * TLD + i]);   // (dqg reused as the Akk accumulator here)
@@ -345,7 +353,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 
   GDN2_TMARK(3);
   // ---- phase 2: A = (I + Akk)^-1 on the transpose (gdn2_fwd.py:173-260)
-  wy_inverse_T128(S, TLD, tmp, t0, p.bc, p.clip);
+  wy_inverse_T128(S, TLD, tmp, t0, p.bc, p.clip, R);
   GDN2_TMARK(4);
   float* at = ws.AT + chunk * C * C;
   for_tile([&](int j, int i) {

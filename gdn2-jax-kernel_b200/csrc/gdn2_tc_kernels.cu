@@ -85,41 +85,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   const float* wt = ws.WT + chunk * C * D;
   const float* u = ws.U + chunk * C * D;
   int g = 0;
-  const Src srcs[3] = {trans(kg, D), direct(wt, C), trans(u, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
-  kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-    mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);         // kg^T W
-    mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);   // kg^T U
-    mma3(tmem + 256, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);   // (kg^T W)^T
-  });
   uint32_t ph = 0;
-  drain(&ts.done, ph, ws.status);
-  // M and M^T leave TMEM row by row as the canonical K-slices the scan
-  // streams with bulk copies (row = TMEM lane, K = column); the scan forms the
-  // lo planes itself (the tensor core reads a float32 word as its tf32 head).
-  float* bo = ws.Bc + chunk * D * D;
-  const float* gl = ws.gcl + chunk * D;
+  // one map per reference chunk: K = its rows (all 128, or 64 per chunk of a
+  // paired tile)
+  const int R = C / p.sub;
 #pragma unroll 1
-  for (int orient = 0; orient < 2; ++orient) {
-    float* mo = ws.M + chunk * 2 * D * D + (size_t)orient * D * D;
-    for_acc<128>(tmem, orient ? 256 : 0, [&](int row, int c, const float* v) {
-      const float dec = __expf(gl[row]);
-      float* sl = mo + (c / KS) * SLICE_FLOATS;
+  for (int hf = 0; hf < p.sub; ++hf) {
+    const int r0 = hf * R;
+    const Src srcs[3] = {trans(kg + r0 * D, D), direct(wt + r0, C), trans(u + r0 * D, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
+    auto issue = [&](int buf, int s) {
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0);         // kg^T W
+      mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);   // kg^T U
+      mma3(tmem + 256, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);   // (kg^T W)^T
+    };
+    if (p.sub == 1) kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, issue);
+    else kloop_pf<false, 2>(ring, g, ws.status, srcs, NoExtra{}, issue);
+    drain(&ts.done, ph, ws.status);
+    // M and M^T leave TMEM row by row as the canonical K-slices the scan
+    // streams with bulk copies (row = TMEM lane, K = column); the scan forms
+    // the lo planes itself (the tensor core reads a float32 word as its tf32
+    // head).
+    const size_t sc = chunk * p.sub + hf;   // reference chunk
+    float* bo = ws.Bc + sc * D * D;
+    const float* gl = ws.gcl + sc * D;
+#pragma unroll 1
+    for (int orient = 0; orient < 2; ++orient) {
+      float* mo = ws.M + sc * 2 * D * D + (size_t)orient * D * D;
+      for_acc<128>(tmem, orient ? 256 : 0, [&](int row, int c, const float* v) {
+        const float dec = __expf(gl[row]);
+        float* sl = mo + (c / KS) * SLICE_FLOATS;
 #pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        float4 o = make_float4(-v[j], -v[j + 1], -v[j + 2], -v[j + 3]);
-        if (row == c + j) o.x += dec;
-        if (row == c + j + 1) o.y += dec;
-        if (row == c + j + 2) o.z += dec;
-        if (row == c + j + 3) o.w += dec;
-        st4f(sl + canon_off(row, c % KS + j, KS) / 4, o);
-      }
+        for (int j = 0; j < 16; j += 4) {
+          float4 o = make_float4(-v[j], -v[j + 1], -v[j + 2], -v[j + 3]);
+          if (row == c + j) o.x += dec;
+          if (row == c + j + 1) o.y += dec;
+          if (row == c + j + 2) o.z += dec;
+          if (row == c + j + 3) o.w += dec;
+          st4f(sl + canon_off(row, c % KS + j, KS) / 4, o);
+        }
+      });
+    }
+    for_acc<128>(tmem, 128, [&](int row, int c, const float* v) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        st4f(bo + row * D + c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
     });
+    // every thread's TMEM reads are complete before the next chunk's MMAs
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
   }
-  for_acc<128>(tmem, 128, [&](int row, int c, const float* v) {
-#pragma unroll
-    for (int j = 0; j < 16; j += 4)
-      st4f(bo + row * D + c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-  });
   tc_teardown(tmem, 512);
 }
 
@@ -167,11 +182,12 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = ts.tmem;
-  const int nt = p.nc * (D / KS);   // slices over the whole scan
+  const int ncs = p.ncs();          // state steps: one per reference chunk
+  const int nt = ncs * (D / KS);   // slices over the whole scan
   auto issue = [&](int t) {          // thread 0 only
     const int it = t / (D / KS), s = t % (D / KS);
-    const int c = BWD ? p.nc - 1 - it : it;
-    const float* src = ws.M + (bh * p.nc + c) * 2 * D * D + (BWD ? D * D : 0) + s * SLICE_FLOATS;
+    const int c = BWD ? ncs - 1 - it : it;
+    const float* src = ws.M + (bh * ncs + c) * 2 * D * D + (BWD ? D * D : 0) + s * SLICE_FLOATS;
     const int slot = t % kScanSlots;
     mbar_arrive_expect_tx(&ts.full[slot], kScanSliceBytes);
     bulk_g2s(sm + slot * SLICE_FLOATS, src, kScanSliceBytes, &ts.full[slot]);
@@ -185,7 +201,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   // initial state (transposed): PROD -> I, else san(init) or 0
   const float* src0 = init ? init + bh * D * D : nullptr;
   if (!BWD && !PROD) {
-    float* hp = ws.hpre + (bh * p.nc) * D * D;
+    float* hp = ws.hpre + (bh * ncs) * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) hp[e] = src0 ? san(src0[e], p.clip) : 0.f;
   }
   // Backward guard.  The affine step replaces the reference's
@@ -224,9 +240,9 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
 
   uint32_t ph = 0;
   float addv[64];
-  for (int it = 0; it < p.nc; ++it) {
-    const int c = BWD ? p.nc - 1 - it : it;
-    const size_t chunk = bh * p.nc + c;
+  for (int it = 0; it < ncs; ++it) {
+    const int c = BWD ? ncs - 1 - it : it;
+    const size_t chunk = bh * ncs + c;
     if (!PROD) {   // this thread's share of the constant term (row v, 64 columns d)
       const float* add = (BWD ? ws.E : ws.Bc) + chunk * D * D;
 #pragma unroll
@@ -277,7 +293,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
         const int t = it * (D / KS) + s + kScanSlots;
         if (t < nt) issue(t);
       }
-    const bool last = it == p.nc - 1;
+    const bool last = it == ncs - 1;
     smax = 0.f;
     float* dst;
     if (PROD) dst = last ? out_final + bh * D * D : nullptr;
@@ -306,7 +322,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     tmem_st_wait();
     if (kGuard) publish_max((it + 1) & 1);
   }
-  if (kGuard && threadIdx.x == 0) ws.bnd[bh * p.nc * 4 + 3] = flagged ? 1.f : 0.f;
+  if (kGuard && threadIdx.x == 0) ws.bnd[bh * ncs * 4 + 3] = flagged ? 1.f : 0.f;
   if (clipped) atomicOr(ws.status + (BWD ? 2 : 1), 1);
   if (!BWD && !PROD && p.diag && out_final) dhf.flush(ws.status, kDiagHFinal);
   if (kGuard && flagged && threadIdx.x == 0) atomicOr(ws.status + 3, 1);
@@ -332,13 +348,19 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   Ring ring = make_ring(sm, &ts, 3);
   const float* wt = ws.WT + chunk * C * D;
   const float* qgt = ws.qgT + chunk * C * D;
-  const float* hp = ws.hpre + chunk * D * D;
   int g = 0;
-  {
-    const Src srcs[3] = {trans(wt, C), trans(qgt, C, p.scale), trans(hp, D)};  // W, s qg, h^T
+  // one K loop per reference chunk of the tile, each with that chunk's entry
+  // state and the other chunk's rows of W and qg masked (paired tiles)
+  const int R = C / p.sub;
+#pragma unroll 1
+  for (int hf = 0; hf < p.sub; ++hf) {
+    const float* hp = ws.hpre + (chunk * p.sub + hf) * D * D;
+    const int lo = hf * R, hi = lo + R;
+    const Src srcs[3] = {rows(trans(wt, C), lo, hi), rows(trans(qgt, C, p.scale), lo, hi),
+                         trans(hp, D)};  // W, s qg, h^T
     kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
-      mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // (W h)^T: (v, i)
-      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg h: (i, v)
+      mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0 || hf > 0);        // (W h)^T: (v, i)
+      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);  // scale qg h: (i, v)
     });
   }
   uint32_t ph = 0;

@@ -196,15 +196,47 @@ struct Src {
   long ld;
   float sc;
   bool trans;
-  float clip;   // > 0: the staged values are sanitised to +-clip (after scaling)
+  float clip;     // > 0: the staged values are sanitised to +-clip (after scaling)
+  int rlo, rhi;   // tile rows outside [rlo, rhi) are staged as zeros (not loaded)
 };
-__device__ __forceinline__ Src direct(const float* p, long ld, float sc = 1.f) { return Src{p, ld, sc, false, 0.f}; }
+__device__ __forceinline__ Src direct(const float* p, long ld, float sc = 1.f) {
+  return Src{p, ld, sc, false, 0.f, 0, 128};
+}
 __device__ __forceinline__ Src trans(const float* p, long ld, float sc = 1.f, float clip = 0.f) {
-  return Src{p, ld, sc, true, clip};
+  return Src{p, ld, sc, true, clip, 0, 128};
+}
+// Only tile rows [lo, hi) (multiples of 8) of the source (one chunk of a
+// paired tile).
+__device__ __forceinline__ Src rows(Src s, int lo, int hi) {
+  s.rlo = lo;
+  s.rhi = hi;
+  return s;
 }
 __device__ __forceinline__ void src_load(const Src& s, int k0, Frag& f) {
-  if (s.trans) load_trans(f, s.p, s.ld, k0);
-  else load_direct(f, s.p, s.ld, k0);
+  if (s.rlo == 0 && s.rhi == 128) {
+    if (s.trans) load_trans(f, s.p, s.ld, k0);
+    else load_direct(f, s.p, s.ld, k0);
+    return;
+  }
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int e = threadIdx.x;
+  if (s.trans) {   // the thread's 4 tile rows rb*4 .. rb*4+3
+    const int rb = (e & 7) + ((e >> 5) & 3) * 8;
+    const int kb = ((e >> 3) & 3) + (e >> 7) * 4;
+    const bool in = rb * 4 >= s.rlo && rb * 4 < s.rhi;
+    const float* p = s.p + (long)(k0 + kb * 4) * s.ld + rb * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f.v[j] = in ? *reinterpret_cast<const float4*>(p + j * s.ld) : z;
+  } else {
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int x = e + it * kThreads;
+      const int lane = x & 31, w = x >> 5;
+      const int r = (w & 15) * 8 + (lane & 7);
+      const int c = ((w >> 4) * 4 + (lane >> 3)) * 4;
+      f.v[it] = (r >= s.rlo && r < s.rhi) ? *reinterpret_cast<const float4*>(s.p + r * s.ld + k0 + c) : z;
+    }
+  }
 }
 __device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, const Frag& f) {
   Frag g = f;
@@ -228,17 +260,17 @@ __device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, co
 // The slice loop is rolled (one copy of its body: the kernels run each K loop
 // once per chunk, so unrolled copies cost instruction-cache misses); the
 // register double buffer advances by copying the prefetched slice.
-template <int NOP, class Ex, class Is>
+template <int NS, int NOP, class Ex, class Is>
 __device__ __forceinline__ void kloop_pf_unrolled(Ring& ring, int& g, int* err,
                                                   const Src (&src)[NOP], Ex extra, Is issue) {
   Frag fa[NOP], fb[NOP];
 #pragma unroll
   for (int o = 0; o < NOP; ++o) src_load(src[o], 0, fa[o]);
 #pragma unroll
-  for (int s = 0; s < 128 / KS; ++s) {
+  for (int s = 0; s < NS; ++s) {
     Frag* cur = (s & 1) ? fb : fa;
     Frag* nxt = (s & 1) ? fa : fb;
-    if (s + 1 < 128 / KS) {
+    if (s + 1 < NS) {
 #pragma unroll
       for (int o = 0; o < NOP; ++o) src_load(src[o], (s + 1) * KS, nxt[o]);
     }
@@ -258,12 +290,14 @@ __device__ __forceinline__ void kloop_pf_unrolled(Ring& ring, int& g, int* err,
 
 // ROLL = false: the slice loop fully unrolled (measured faster for the short
 // kernels whose K loops carry few operands: affine, fwd_out, bwd_prep, and the
-// dv / dqg loops of bwd_intra1).
-template <bool ROLL = true, int NOP, class Ex, class Is>
+// dv / dqg loops of bwd_intra1).  NS: 32-wide K slices (4 = K of 128; 2 = one
+// 64-row chunk of a paired tile, unrolled form only).
+template <bool ROLL = true, int NS = 128 / KS, int NOP, class Ex, class Is>
 __device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src (&src)[NOP],
                                          Ex extra, Is issue) {
+  static_assert(NS == 128 / KS || !ROLL, "partial K loops are unrolled");
   if (!ROLL) {
-    kloop_pf_unrolled(ring, g, err, src, extra, issue);
+    kloop_pf_unrolled<NS>(ring, g, err, src, extra, issue);
     return;
   }
   Frag cur[NOP], nxt[NOP];

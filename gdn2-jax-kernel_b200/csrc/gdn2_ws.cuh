@@ -3,6 +3,9 @@
 // Every per-chunk tile is stored contiguously at offset
 // chunk_id * tile_elems, chunk_id = (b*H + h)*nc + c, in float32.  Tiles are
 // stored in the orientation their consumer streams into shared memory.
+// Arrays of the state recurrence (gcl, hpre, M, Bc, bnd, E, dh) hold one
+// entry per reference chunk: index chunk_id * sub + half when a tile carries
+// sub = 2 chunks of 64 rows.
 #pragma once
 #include <stddef.h>
 #include <stdint.h>
@@ -10,12 +13,15 @@
 namespace gdn2 {
 
 struct Problem {
-  int B, T, H, D, C, nc;   // C = chunk length BT, nc = T / C
+  int B, T, H, D, C, nc;   // C = kernel tile rows, nc = T / C
+  int sub;                 // reference chunks per tile: 1, or 2 (two BT = 64 chunks
+                           // stacked in one 128-row tensor-core tile)
   int bc;                  // the reference's sub-block BC (clip granularity of B4)
   int diag;                // 1: accumulate per-stage diagnostics in the status header
   int gates;               // 1: w, b, g are pre-activations (GDN2_GATES_RAW)
   float scale, clip;
   __host__ __device__ long row_stride() const { return (long)H * D; }
+  __host__ __device__ int ncs() const { return nc * sub; }   // reference chunks per (b, h)
 };
 
 // Float offsets (per chunk multiples) of every workspace array.
@@ -58,18 +64,19 @@ struct Workspace {
   int* status;   // device status word (1 = a bounded wait timed out), zeroed by every entry point
   size_t bytes;
 
-  static size_t per_chunk_floats(int C, int D, bool bwd) {
-    size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + D;   // forward
-    f += (size_t)D * D + (size_t)C * D;                        // residuals
-    f += 3 * (size_t)D * D;                                    // M (both ways), Bc
-    f += 4;                                                    // bnd
-    if (bwd) f += 2 * (size_t)C * C + 7 * (size_t)C * D + 2 * (size_t)D * D;
+  static size_t per_chunk_floats(int C, int D, bool bwd, int sub = 1) {
+    const size_t S = (size_t)sub;
+    size_t f = 2 * (size_t)C * C + 5 * (size_t)C * D + S * D;   // forward
+    f += S * D * D + (size_t)C * D;                              // residuals
+    f += S * 3 * D * D;                                          // M (both ways), Bc
+    f += S * 4;                                                  // bnd
+    if (bwd) f += 2 * (size_t)C * C + 7 * (size_t)C * D + S * 2 * D * D;
     return f;
   }
-  static size_t required_bytes(int B, int H, int nc, int C, int D, bool bwd) {
-    return per_chunk_floats(C, D, bwd) * (size_t)B * H * nc * sizeof(float) + 512;
+  static size_t required_bytes(int B, int H, int nc, int C, int D, bool bwd, int sub = 1) {
+    return per_chunk_floats(C, D, bwd, sub) * (size_t)B * H * nc * sizeof(float) + 512;
   }
-  static Workspace carve(void* p, int B, int H, int nc, int C, int D, bool bwd) {
+  static Workspace carve(void* p, int B, int H, int nc, int C, int D, bool bwd, int sub = 1) {
     Workspace w{};
     size_t n = (size_t)B * H * nc;
     float* f = reinterpret_cast<float*>(((uintptr_t)p + 255) & ~(uintptr_t)255);
@@ -84,15 +91,16 @@ struct Workspace {
     w.kg = take((size_t)C * D);
     w.qgT = take((size_t)C * D);
     w.gc = take((size_t)C * D);
-    w.gcl = take((size_t)D);
-    w.hpre = take((size_t)D * D);
+    const size_t S = (size_t)sub;
+    w.gcl = take(S * D);
+    w.hpre = take(S * D * D);
     w.vnew = take((size_t)C * D);
-    w.M = take(2 * (size_t)D * D);
-    w.Bc = take((size_t)D * D);
-    w.bnd = take(4);
+    w.M = take(S * 2 * D * D);
+    w.Bc = take(S * D * D);
+    w.bnd = take(S * 4);
     if (bwd) {
       w.dv = take((size_t)C * D);
-      w.dh = take((size_t)D * D);
+      w.dh = take(S * D * D);
       w.dAqkT = take((size_t)C * C);
       w.dAkkT = take((size_t)C * C);
       w.dWp = take((size_t)C * D);
@@ -100,10 +108,10 @@ struct Workspace {
       w.pdk = take((size_t)C * D);
       w.pdb = take((size_t)C * D);
       w.pdgc = take((size_t)C * D);
-      w.E = take((size_t)D * D);
+      w.E = take(S * D * D);
       w.dvp = take((size_t)C * D);
     }
-    w.bytes = required_bytes(B, H, nc, C, D, bwd);
+    w.bytes = required_bytes(B, H, nc, C, D, bwd, sub);
     return w;
   }
 };

@@ -43,6 +43,7 @@ SIGNATURES = {
     "gdn2_copy_heads": (_i, [_vp, _vp, ctypes.c_long, _i, _i, _i, _sz, _i, _vp]),
     "gdn2_selftest_wait_timeout": (_i, [_vp, _sz, _i, _vp]),
     "gdn2_diag_enable": (_i, [_i]),
+    "gdn2_pair64_enable": (_i, [_i]),
     "gdn2_diag_read": (_i, [_vp, _sz, _vp, _i, ctypes.POINTER(ctypes.c_int),
                             ctypes.POINTER(ctypes.c_float)]),
 }

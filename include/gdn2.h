@@ -127,6 +127,12 @@ int gdn2_workspace_status(const void* workspace, size_t workspace_bytes, void* s
  * 6 kernel_C_qg, 7 kernel_D_o, 8 kernel_D_h_final and returns the number of
  * stages (9).  Values describe the latest call on that workspace. */
 int gdn2_diag_enable(int on);
+/* BT = 64 with D = 128 on the tensor-core kernels: two chunks per 128-row
+ * tile (block-diagonal chunk scores and WY solve, gates and gc_last per
+ * chunk, one state step per chunk), the same function as the BT = 64
+ * CUDA-core kernels.  Needs T % 128 == 0 (otherwise the CUDA-core kernels
+ * run).  Returns the previous setting. */
+int gdn2_pair64_enable(int on);
 int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
                    int* nonfinite, float* maxabs);
 

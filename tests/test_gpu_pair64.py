@@ -1,0 +1,108 @@
+"""BT = 64 on the tensor-core kernels: two 64-row chunks per 128-row tile.
+
+The paired tiles must compute the reference's BT = 64 function (block-
+diagonal chunk scores and WY solve, gc, kg and gc_last per chunk, one state
+step per chunk), so every check here is against the float64 oracle at
+BT = 64, against the reference's own golden vectors, and against the
+CUDA-core BT = 64 kernels on the same inputs.  Tolerances (rel-L2): 1e-4
+for float32 inputs, 2e-2 for bfloat16.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import gdn2_oracle as O
+from conftest import cuda_ok
+from gdn2_package import _lib, gdn2_fwd, gdn2_pallas_forward
+from gdn2_package.synthetic import make_inputs
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+NAMES = ("q", "k", "v", "w", "b", "g")
+TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def rel(a, b):
+    a = torch.as_tensor(a).double().cpu()
+    b = torch.as_tensor(b).double().cpu()
+    return float((a - b).norm() / max(float(b.norm()), 1e-300))
+
+
+@pytest.fixture
+def paired():
+    lib = _lib.load()
+    prev = lib.gdn2_pair64_enable(1)
+    yield lib
+    lib.gdn2_pair64_enable(prev)
+
+
+def _set(BT, BC, clip):
+    gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP = BT, BC, clip
+
+
+def _both_paths(lib, fn):
+    """fn() with the paired tensor-core tiles, then with the CUDA-core kernels."""
+    lib.gdn2_pair64_enable(1)
+    a = fn()
+    lib.gdn2_pair64_enable(0)
+    b = fn()
+    lib.gdn2_pair64_enable(1)
+    return a, b
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,T,H,BC,h0s", [
+    (1, 256, 2, 16, None),
+    (2, 512, 3, 16, 0.1),
+    (1, 384, 2, 32, 0.1),
+    (1, 256, 2, 64, 0.1),
+])
+def test_forward_vs_oracle(paired, B, T, H, BC, h0s, dtype):
+    _set(64, BC, 1e4)
+    inp = make_inputs(B, T, H, 128, seed=5, h0_std=h0s)
+    args = [torch.as_tensor(inp[n]).to("cuda", dtype) for n in NAMES]
+    h0 = torch.as_tensor(inp["h0"]).cuda() if "h0" in inp else None
+    (o, h), (o2, h2) = _both_paths(paired, lambda: gdn2_pallas_forward(*args, inp["scale"], h0))
+    ref_in = [torch.as_tensor(inp[n]).to(dtype).double().numpy() for n in NAMES]
+    o_r, h_r = O.forward(*ref_in, inp["scale"], inp.get("h0"), 64, BC, 1e4)
+    tol = TOL[dtype]
+    assert rel(o, o_r) < tol and rel(h, h_r) < tol, (rel(o, o_r), rel(h, h_r))
+    # the two kernel families agree far inside the tolerance
+    assert rel(o, o2) < 1e-5 and rel(h, h2) < 1e-5, (rel(o, o2), rel(h, h2))
+
+
+@pytest.mark.parametrize("name", ["ref_bt64_bc32", "ref_ones_bt64_bc32"])
+def test_forward_reference_golden(paired, name):
+    """The reference source's own outputs; the all-ones case (g = +1) takes
+    the exact elementwise scores with the +-20 clip and saturates CLIP."""
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    B, T, H, D, BT, BC = (int(x) for x in z["meta"])
+    _set(BT, BC, float(z["clip"]))
+    args = [torch.as_tensor(z[n]).cuda() for n in NAMES]
+    h0 = torch.as_tensor(z["h0"]).cuda()
+    o, h = gdn2_pallas_forward(*args, float(z["scale"]), h0)
+    assert rel(o, z["o"]) < 1e-4 and rel(h, z["h_final"]) < 1e-4, (rel(o, z["o"]),
+                                                                    rel(h, z["h_final"]))
+
+
+@pytest.mark.parametrize("clip,h0s,gscale", [
+    (0.3, 0.1, 1.0),     # U, W, kg, o clip
+    (0.5, 0.1, 0.01),    # slow gates: the state itself clips between chunks
+])
+def test_forward_with_clip_active(paired, clip, h0s, gscale):
+    """CLIP acting inside and between the two chunks of a tile: the state
+    must be sanitised after each 64-row chunk, as the reference does."""
+    _set(64, 16, clip)
+    inp = make_inputs(2, 768, 2, 128, seed=31, h0_std=h0s)
+    inp["g"] = inp["g"] * np.float32(gscale)
+    args = [torch.as_tensor(inp[n]).cuda() for n in NAMES]
+    h0 = torch.as_tensor(inp["h0"]).cuda()
+    (o, h), (o2, h2) = _both_paths(paired, lambda: gdn2_pallas_forward(*args, inp["scale"], h0))
+    o_r, h_r = O.forward(*[inp[n].astype(np.float64) for n in NAMES], inp["scale"], inp["h0"],
+                         64, 16, clip)
+    assert rel(o, o_r) < 1e-4 and rel(h, h_r) < 1e-4, (rel(o, o_r), rel(h, h_r))
+    assert rel(o, o2) < 1e-5 and rel(h, h2) < 1e-5, (rel(o, o2), rel(h, h2))
