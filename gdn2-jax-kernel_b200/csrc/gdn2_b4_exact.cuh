@@ -32,16 +32,18 @@ __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
                                const float* __restrict__ dAkkT, const float* pdq, const float* pdk,
                                const float* pdb, const float* pdgc, T* dq_out, T* dk_out,
                                T* db_out, long off, float* sdg, float scale, float clip,
-                               int gates) {
-  const int nsub = C / BC;
+                               int gates, int span) {
+  // span: rows of one reference chunk (C, or C / 2 for a tile of two chunks);
+  // the pairs stay inside the chunk of row x
+  const int nsc = span / BC;
   for (int e = threadIdx.x; e < C * D; e += kThreads) {
-    const int x = e / D, d = e % D, X = x / BC;
+    const int x = e / D, d = e % D, X = x / BC, X0 = (X / nsc) * nsc;
     const float kx = to_f<T>(kc[x * rs + d]), bx = ld_gate<T>(bc + x * rs + d, gates, kGateB);
     const float lqx = scale * to_f<T>(qc[x * rs + d]), lkx = bx * kx;
     const float gx = gc[x * gld + d];
     float dq = 0.f, dbk = 0.f, dk = 0.f, dgc = 0.f;
-    for (int si = X; si < nsub; ++si) {
-      for (int sj = 0; sj <= si; ++sj) {
+    for (int si = X; si < X0 + nsc; ++si) {
+      for (int sj = X0; sj <= si; ++sj) {
         if (si != X && sj != X) continue;
         float dlq = 0.f, dlk = 0.f, wqi = 0.f, wki = 0.f;
         float drq = 0.f, drk = 0.f, wqj = 0.f, wkj = 0.f;

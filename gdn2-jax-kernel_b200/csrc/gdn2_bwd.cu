@@ -20,7 +20,8 @@ constexpr float kFinalClip = 1e4f;   // gdn2_pipeline.py:34
 template <int C, int D, int NV>
 __global__ void __launch_bounds__(kThreads, 2)
 k_bwd_state(Problem p, Workspace ws, const float* __restrict__ dout,
-            const float* __restrict__ dh_final, float* __restrict__ dh0, bool only_flagged) {
+            const float* __restrict__ dh_final, float* __restrict__ dh0, bool only_flagged,
+            bool pair) {
   using T1 = typename TileFor<C, NV>::type;
   using T3 = typename TileFor<D, NV>::type;
   constexpr int LDC = C + 4, LDD = D + 4;
@@ -39,11 +40,17 @@ k_bwd_state(Problem p, Workspace ws, const float* __restrict__ dout,
     const int d = e / NV, vv = e % NV;
     sdh[e] = dh_final ? san(dh_final[bh * D * D + d * D + v0 + vv], p.clip) : 0.f;
   }
+  // pair: 64-row chunks of the tensor-core workspace, two per 128-row tile;
+  // the row-major arrays (kg, dv) line up with 64-row chunks, the transposed
+  // tile arrays (Aqk^T, qg^T, W^T) are read at the tile's row stride.
+  const long tld = pair ? 2 * C : C;
   for (int c = p.nc - 1; c >= 0; --c) {
     const size_t chunk = bh * p.nc + c;
+    const size_t tile = pair ? chunk >> 1 : chunk;
+    const int hoff = pair ? (int)(chunk & 1) * C : 0;
     const float* doc = dout + ((long)bb * p.T + (long)c * C) * rs + (long)h * D + v0;
     load_tile<float>(sdo, NV, doc, rs, C, NV);
-    load_tile_T<float>(X, LDC, ws.AqkT + chunk * C * C, C, C, C);   // X[i][j] = Aqk(i,j)
+    load_tile_T<float>(X, LDC, ws.AqkT + tile * tld * tld + hoff * tld + hoff, tld, C, C);   // X[i][j] = Aqk(i,j)
     __syncthreads();
     T1 tp;
     tp.zero();
@@ -68,13 +75,13 @@ k_bwd_state(Problem p, Workspace ws, const float* __restrict__ dout,
       }
     }
     __syncthreads();
-    load_tile_T<float>(X, LDD, ws.qgT + chunk * C * D, C, D, C);    // X[i][d] = qg(i,d)
+    load_tile_T<float>(X, LDD, ws.qgT + tile * tld * D + hoff, tld, D, C);    // X[i][d] = qg(i,d)
     __syncthreads();
     T3 ta;
     ta.zero();
     ta.mma(X, LDD, sdo, NV, 0, C);
     __syncthreads();
-    load_tile_T<float>(X, LDD, ws.WT + chunk * C * D, C, D, C);     // X[i][d] = W(i,d)
+    load_tile_T<float>(X, LDD, ws.WT + tile * tld * D + hoff, tld, D, C);     // X[i][d] = W(i,d)
     __syncthreads();
     {
       T3 tb;
@@ -570,7 +577,7 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
   if (run_exact) {
     // the reference's pair order (overwrites the fast path's outputs)
     b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, D, dAqkT, dAkkT, pdq, pdk, pdb, pdgc,
-                      dq_out, dk_out, db_out, off, sdg, p.scale, p.clip, GATES);
+                      dq_out, dk_out, db_out, off, sdg, p.scale, p.clip, GATES, C);
   }
   __syncthreads();
   column_revcumsum<C, D>(sdg, red);
@@ -586,13 +593,14 @@ k_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
 template <int C, int D>
 cudaError_t launch_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
                              const float* dh_final, float* dh0, cudaStream_t s,
-                             bool only_flagged) {
+                             bool only_flagged, bool pair) {
   constexpr int NV = 32;
   const size_t smem = StateSmem<C, D, NV>::bytes();
   auto kern = k_bwd_state<C, D, NV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(D / NV, p.H, p.B), kThreads, smem, s>>>(p, ws, dout, dh_final, dh0, only_flagged);
+  kern<<<dim3(D / NV, p.H, p.B), kThreads, smem, s>>>(p, ws, dout, dh_final, dh0, only_flagged,
+                                                       pair);
   return cudaGetLastError();
 }
 
@@ -642,7 +650,7 @@ cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, con
 
 #define GDN2_INST_BSTATE(C, D)                                                               \
   template cudaError_t launch_bwd_state<C, D>(const Problem&, const Workspace&, const float*, \
-                                              const float*, float*, cudaStream_t, bool);
+                                              const float*, float*, cudaStream_t, bool, bool);
 #define GDN2_INST_BINTRA(T, C, D)                                                            \
   template cudaError_t launch_bwd_intra<T, C, D>(                                            \
       const T*, const T*, const T*, const T*, const T*, const T*, const float*, const float*, \

@@ -27,7 +27,7 @@ struct Profiler {
 Profiler g_prof;
 std::mutex g_prof_mu;
 int g_diag = 0;   // per-stage diagnostics on (gdn2_diag_enable)
-int g_pair64 = 0;  // BT = 64 chunks paired into 128-row tensor-core tiles (gdn2_pair64_enable)
+int g_pair64 = 1;  // BT = 64 chunks paired into 128-row tensor-core tiles (gdn2_pair64_enable)
 
 void prof_hook(int stage, int end, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -62,7 +62,7 @@ int cuda_fail(cudaError_t e, const char* where) {
 }
 
 int validate(int dtype, int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
-  dtype &= ~GDN2_GATES_RAW;
+  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR);
   if (dtype != GDN2_F32 && dtype != GDN2_BF16)
     return fail(GDN2_ERR_INVALID, "unsupported dtype code %s%ld", "", dtype);
   if (B <= 0 || T <= 0 || H <= 0)
@@ -321,12 +321,12 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  const bool pair = use_pair64(T, D, BT) && !save_residuals;   // TODO backward
+  const bool pair = use_pair64(T, D, BT) && !(dtype & GDN2_NO_PAIR);
   const int KT = pair ? 128 : BT;   // kernel tile rows
   Problem p = make_problem(B, T, H, D, KT, BC, scale, clip);
   p.sub = pair ? 2 : 1;
   p.gates = (dtype & GDN2_GATES_RAW) != 0;
-  dtype &= ~GDN2_GATES_RAW;
+  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR);
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, KT, D, false, p.sub);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;
@@ -355,38 +355,42 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
                 (long)need, (long)workspace_bytes);
-  Problem p = make_problem(B, T, H, D, BT, BC, scale, clip);
+  // the same kernel family as the forward that left the residuals
+  const bool pair = use_pair64(T, D, BT) && !(dtype & GDN2_NO_PAIR);
+  const int KT = pair ? 128 : BT;   // kernel tile rows
+  Problem p = make_problem(B, T, H, D, KT, BC, scale, clip);
+  p.sub = pair ? 2 : 1;
   p.gates = (dtype & GDN2_GATES_RAW) != 0;
-  dtype &= ~GDN2_GATES_RAW;
-  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, BT, D, true);
+  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR);
+  const Workspace ws = Workspace::carve(workspace, B, H, p.nc, KT, D, true, p.sub);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;
   if (!residuals_valid) {
     // The reference's custom_vjp keeps only the inputs and recomputes the
     // forward in the backward (gdn2_pipeline.py:64-83); o is not needed.
     rc = dtype == GDN2_F32
-             ? run_fwd_intra<float>(BT, D, q, k, v, w, b, g, p, ws, s)
-             : run_fwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, p, ws, s);
+             ? run_fwd_intra<float>(KT, D, q, k, v, w, b, g, p, ws, s)
+             : run_fwd_intra<__nv_bfloat16>(KT, D, q, k, v, w, b, g, p, ws, s);
     if (rc) return rc;
-    if (use_tc(BT, D)) {
+    if (use_tc(KT, D)) {
       cudaError_t e = launch_tc_fwd(p, ws, h0, nullptr, nullptr, s, hook());
       if (e != cudaSuccess) return cuda_fail(e, "tc_fwd");
     } else {
-      rc = run_fwd_state(BT, D, p, ws, h0, nullptr, nullptr, 1, s);
+      rc = run_fwd_state(KT, D, p, ws, h0, nullptr, nullptr, 1, s);
       if (rc) return rc;
     }
   }
-  if (use_tc(BT, D)) {
+  if (use_tc(KT, D)) {
     cudaError_t e = launch_tc_bwd_state(p, ws, dout, dh_final, dh0, s, hook());
     if (e != cudaSuccess) return cuda_fail(e, "tc_bwd_state");
   } else {
-    rc = run_bwd_state(BT, D, p, ws, dout, dh_final, dh0, s);
+    rc = run_bwd_state(KT, D, p, ws, dout, dh_final, dh0, s);
     if (rc) return rc;
   }
   return dtype == GDN2_F32
-             ? run_bwd_intra<float>(BT, D, q, k, v, w, b, g, dout, dh_final, dq, dk, dv, dw,
+             ? run_bwd_intra<float>(KT, D, q, k, v, w, b, g, dout, dh_final, dq, dk, dv, dw,
                                     db, dg, p, ws, s)
-             : run_bwd_intra<__nv_bfloat16>(BT, D, q, k, v, w, b, g, dout, dh_final, dq, dk,
+             : run_bwd_intra<__nv_bfloat16>(KT, D, q, k, v, w, b, g, dout, dh_final, dq, dk,
                                             dv, dw, db, dg, p, ws, s);
 }
 

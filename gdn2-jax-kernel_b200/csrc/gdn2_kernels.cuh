@@ -381,7 +381,7 @@ cudaError_t launch_fwd_state(const Problem& p, const Workspace& ws, const float*
 template <int C, int D>
 cudaError_t launch_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
                              const float* dh_final, float* dh0, cudaStream_t s,
-                             bool only_flagged = false);
+                             bool only_flagged = false, bool pair = false);
 template <typename T, int C, int D>
 cudaError_t launch_bwd_intra(const T* q, const T* k, const T* v, const T* w, const T* b,
                              const T* g, const float* dout, const float* dh_final, T* dq, T* dk,

@@ -53,7 +53,9 @@ constexpr float kFinalClipTc = 1e4f;   // gdn2_pipeline.py:34
 
 struct TcSmemB {
   float colpart[8][D];   // first member: 16-byte aligned for float4 stores
+  float colpart1[8][D];  // the second chunk's sums (paired tiles)
   float rowdot[D];
+  float rowdot1[D];
   uint64_t bars[2];
   uint64_t done;
   uint32_t tmem;
@@ -260,6 +262,170 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
 }
 
 // ---------------------------------------------------------------------------
+// k_tc_bwd_intra1 for a tile of two 64-row chunks (BT = 64).  Every product
+// that meets a state (h_pre or dh_next of the chunk) runs as one K loop per
+// chunk with the other chunk's rows masked, accumulating in TMEM; dWp is
+// formed transposed, (dk, i) = h_pre (-dv)^T, because the A operand of the
+// single-chunk form (-dv in TMEM) cannot be row-masked.  gc_last, the column
+// sums and the state row dots are per chunk; dAqk is block-diagonal.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
+                     const float* __restrict__ dout, const float* __restrict__ dh_final,
+                     Problem p, Workspace ws) {
+  extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(16) TcSmemB ts;
+  constexpr int R = C / 2;
+  const size_t chunk = blockIdx.x;
+  const int c = (int)(chunk % p.nc);
+  const size_t bh = chunk / p.nc;
+  const int h = (int)(bh % p.H), bb = (int)(bh / p.H);
+  const long rs = p.row_stride();
+  const long off = ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
+  const T *qc = q + off, *kc = k + off;
+  const float* doc = dout + off;
+  const float* gc = ws.gc + chunk * C * D;
+  const float* vnew = ws.vnew + chunk * C * D;
+  const size_t sc0 = chunk * 2;   // first reference chunk of the tile
+  const float* hp[2] = {ws.hpre + sc0 * D * D, ws.hpre + (sc0 + 1) * D * D};
+  const bool last_tile = c + 1 == p.nc;
+  const float* dhn[2] = {ws.dh + (sc0 + 1) * D * D,
+                         last_tile ? dh_final + bh * D * D : ws.dh + (sc0 + 2) * D * D};
+  float *pdq = ws.pdq + chunk * C * D, *pdk = ws.pdk + chunk * C * D,
+        *pdgc = ws.pdgc + chunk * C * D;
+  float* dv = ws.dv + chunk * C * D;
+  const uint32_t tmem = setup(&ts);
+  Ring ring = ring_of(sm, &ts, 2);
+  int g = 0;
+  uint32_t ph = 0;
+  // dv = san(dvp + kg dh_next)  (TMEM 0); only the last chunk of the
+  // sequence sees dh_final, sanitised (gdn2_bwd.py:53)
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const float dclip = (hf == 1 && last_tile) ? p.clip : 0.f;
+    const Src srcs[2] = {rows(direct(ws.kg + chunk * C * D, D), hf * R, hf * R + R),
+                         trans(dhn[hf], D, 1.f, dclip)};   // (i,d), (v,d)
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0 || hf > 0);
+    });
+  }
+  drain(&ts.done, ph, ws.status);
+  {
+    const float* dvp = ws.dvp + chunk * C * D;
+    for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
+      float4 av[4];   // loads first: the dv stores below may alias them for the compiler
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) av[kk] = *reinterpret_cast<const float4*>(dvp + i * D + c0 + 4 * kk);
+#pragma unroll
+      for (int kk = 0; kk < 16; kk += 4) {
+        const float4 a = av[kk / 4];
+        *reinterpret_cast<float4*>(dv + i * D + c0 + kk) =
+            make_float4(san(a.x + x[kk], p.clip), san(a.y + x[kk + 1], p.clip),
+                        san(a.z + x[kk + 2], p.clip), san(a.w + x[kk + 3], p.clip));
+      }
+    });
+  }
+  fence_before_sync();
+  __syncthreads();   // dv in global memory for the staging below; TMEM 0 free
+  fence_after_sync();
+  // dqg = do h_pre^T (i, dk) at TMEM 0; dWp^T = h_pre (-dv)^T (dk, i) at 128
+  ring.nop = 3;
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const Src srcs[3] = {rows(direct(doc, rs), hf * R, hf * R + R), direct(hp[hf], D),
+                         rows(direct(dv, D, -1.f), hf * R, hf * R + R)};   // (i,v) (dk,v) (i,v)
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0 || hf > 0);
+      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);
+    });
+  }
+  // dkg = vnew dh_next^T (j, dk) at TMEM 256 (B3's raw dh_next,
+  // gdn2_pipeline.py:52-56); do vnew^T (i, j) at 384
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const Src srcs[3] = {rows(direct(vnew, D), hf * R, hf * R + R), direct(doc, rs),
+                         direct(dhn[hf], D)};   // (j,v) (i,v) (dk,v)
+    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+      mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);
+      mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0 || hf > 0);
+    });
+  }
+  drain(&ts.done, ph, ws.status);
+  float* t0 = sm;                  // the ring is free: two padded 128 x 128 tiles
+  float* t1 = sm + TILE_FLOATS;
+  float* dwp = ws.dWp + chunk * C * D;
+  for_acc<128>(tmem, 128, [&](int dk, int i0, const float* x) {   // dWp(i, dk), coalesced over dk
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dwp[(i0 + j) * D + dk] = x[j];
+  });
+  acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
+  acc_to_smem<false>(tmem, 256, t1);   // dkg
+  __syncthreads();
+  float cs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for_tile([&](int i, int d) {
+    const int hf = i / R;
+    const float4 x = lds4(t0 + i * TLD + d), y = lds4(t1 + i * TLD + d);
+    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gc + (hf * R + R - 1) * D + d);
+    const float4 eg = exp4(g4);
+    const float4 qv = ld4<T>(qc + i * rs + d), kv = ld4<T>(kc + i * rs + d);
+    const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
+    st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
+        san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
+    const float4 pg = make_float4(dqg.x * (qv.x * eg.x), dqg.y * (qv.y * eg.y),
+                                  dqg.z * (qv.z * eg.z), dqg.w * (qv.w * eg.w));
+    const float4 f = exp4(make_float4(l4.x - g4.x, l4.y - g4.y, l4.z - g4.z, l4.w - g4.w));
+    const float4 xs = make_float4(y.x * (kv.x * f.x), y.y * (kv.y * f.y), y.z * (kv.z * f.z),
+                                  y.w * (kv.w * f.w));
+    st4(pdk + i * D + d, y.x * f.x, y.y * f.y, y.z * f.z, y.w * f.w);
+    st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
+    cs[hf][0] += xs.x; cs[hf][1] += xs.y; cs[hf][2] += xs.z; cs[hf][3] += xs.w;
+  });
+  float* daqkT = ws.dAqkT + chunk * C * C;
+  for_acc<128>(tmem, 384, [&](int i, int c0, const float* v) {   // dAqk^T, coalesced per column
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      daqkT[(c0 + t) * C + i] = (c0 + t <= i && (c0 + t) / R == i / R) ? san(v[t], p.clip) : 0.f;
+  });
+  {
+    const int d = (threadIdx.x & 31) * 4;
+    st4(&ts.colpart[threadIdx.x >> 5][d], cs[0][0], cs[0][1], cs[0][2], cs[0][3]);
+    st4(&ts.colpart1[threadIdx.x >> 5][d], cs[1][0], cs[1][1], cs[1][2], cs[1][3]);
+  }
+  // rowdot[d] = sum_v dh_next(d, v) h_pre(d, v) of each chunk
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll 4
+      for (int rr = 0; rr < D / 8; ++rr) {
+        const int d = warp * (D / 8) + rr;
+        const float4 a = *reinterpret_cast<const float4*>(dhn[hf] + d * D + lane * 4);
+        const float4 h4 = *reinterpret_cast<const float4*>(hp[hf] + d * D + lane * 4);
+        float v = a.x * h4.x + a.y * h4.y + a.z * h4.z + a.w * h4.w;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) (hf ? ts.rowdot1 : ts.rowdot)[d] = v;
+      }
+    }
+  }
+  __syncthreads();
+  // gc_last row of each chunk: sum_i dkg kg + e^{gc_last} sum_v dh_next h_pre
+  // (gdn2_bwd.py:185, 196-201)
+  if (threadIdx.x < D) {
+    const int d = threadIdx.x;
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+      float csum = 0.f;
+      for (int r = 0; r < 8; ++r) csum += (hf ? ts.colpart1 : ts.colpart)[r][d];   // fixed order
+      const int lr = hf * R + R - 1;
+      pdgc[lr * D + d] += csum + __expf(gc[lr * D + d]) * (hf ? ts.rowdot1 : ts.rowdot)[d];
+    }
+  }
+  teardown(tmem);
+}
+
+// ---------------------------------------------------------------------------
 // dA = san(dWp kb^T + dv wv^T); tmp = san(dA A^T); dAkk = -(A^T tmp) * strict;
 // dkb = A^T dWp; dwv = A^T dv -> pdk, pdb, pdgc (sanitised B3 totals), dw, dv,
 // exactly as k_bwd_intra2.  dkb/dwv run first (inputs only); dA then goes from
@@ -449,10 +615,15 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   float* dAkkT = ws.dAkkT + chunk * C * C;
   acc_to_smem<false>(tmem, 0, t0);    // t0[j][i] = acc(j, i)
   __syncthreads();
+  // strictly lower and, for a tile of two chunks, block-diagonal (the 4
+  // columns i of one store lie in one chunk)
+  const int R = C / p.sub;
   for_tile([&](int j, int i) {
     const float4 x = lds4(t0 + j * TLD + i);
-    st4(dAkkT + j * C + i, j < i ? san(-x.x, p.clip) : 0.f, j < i + 1 ? san(-x.y, p.clip) : 0.f,
-        j < i + 2 ? san(-x.z, p.clip) : 0.f, j < i + 3 ? san(-x.w, p.clip) : 0.f);
+    const bool same = j / R == i / R;
+    st4(dAkkT + j * C + i, same && j < i ? san(-x.x, p.clip) : 0.f,
+        same && j < i + 1 ? san(-x.y, p.clip) : 0.f, same && j < i + 2 ? san(-x.z, p.clip) : 0.f,
+        same && j < i + 3 ? san(-x.w, p.clip) : 0.f);
   });
   teardown(tmem);
 }
@@ -529,6 +700,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread || p.bc < 32;
   const int JW = (block_max(spread64, red) <= 80.f && p.bc % 64 == 0) ? 64 : 32;
   bool run_exact = exact;
+  const int R = C / p.sub;   // rows of one reference chunk
   GDN2_TMARK(1);
 
   if (!exact) {
@@ -656,7 +828,9 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           float a[16];
           tmem_ld16(lane_quarter_addr(tmem, 128 * J + c0), a);
           const int r = JW * J;
-          const bool use = left ? (x >= r) : (x < r + JW);
+          // same chunk only (paired tiles): across chunks the gc are of
+          // different chunks and the factor below is meaningless
+          const bool use = (left ? (x >= r) : (x < r + JW)) && x / R == r / R;
           if (use) {
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
@@ -779,11 +953,11 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     // the reference's pair order: positive gates, wide gate spreads, BC < 32,
     // or a chunk whose guard failed (its fast-path outputs are overwritten)
     b4_exact_chunk<T>(C, D, p.bc, qc, kc, bc, rs, gc, GLD, dAqkT, dAkkT, pdq, pdk, pdb, pdgc, dq_out,
-                      dk_out, db_out, off, sdg, p.scale, p.clip, GATES);
+                      dk_out, db_out, off, sdg, p.scale, p.clip, GATES, R);
   }
   GDN2_TMARK(10);
   __syncthreads();
-  column_revcumsum<C, D>(sdg, red);
+  column_revcumsum<C, D>(sdg, red, p.sub == 2);
   for_tile([&](int i, int d) {
     const float4 v4 = ldg4(sdg + i * D + d);
     float4 dgo = san4(san4(v4, p.clip), kFinalClipTc);
@@ -841,8 +1015,12 @@ cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w
   if ((e = cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
       cudaSuccess)
     return e;
+  if ((e = cudaFuncSetAttribute(k_tc_bwd_intra1_pair<T>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+    return e;
   hook.begin(kStageBwdIntra1, s);
-  k_tc_bwd_intra1<T><<<nchunks, kThreads, smem, s>>>(q, k, dout, dh_final, p, ws);
+  if (p.sub == 2) k_tc_bwd_intra1_pair<T><<<nchunks, kThreads, smem, s>>>(q, k, dout, dh_final, p, ws);
+  else k_tc_bwd_intra1<T><<<nchunks, kThreads, smem, s>>>(q, k, dout, dh_final, p, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdIntra1, s);
   hook.begin(kStageBwdIntra2, s);

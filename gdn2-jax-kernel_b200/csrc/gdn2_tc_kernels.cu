@@ -429,7 +429,10 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   const int c = (int)(chunk % p.nc);
   const size_t bh = chunk / p.nc;
   const int h = (int)(bh % p.H), bb = (int)(bh / p.H);
-  const uint32_t tmem = tc_setup(&ts, 256);
+  const uint32_t tmem = tc_setup(&ts, 512);
+  // E of reference chunk hf accumulates at TMEM 128 + 128 hf; its K rows are
+  // the slices [hf * NSC, (hf + 1) * NSC)
+  const int NSC = 4 / p.sub;
   Ring ring = make_ring(sm, &ts, 3);
   const long rs = p.row_stride();
   const float* doc = dout + ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
@@ -440,7 +443,8 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
     const Src srcs[3] = {direct(aqkt, C), direct(qgt, C, p.scale), trans(doc, rs)};  // (j,i) (d,i) (v,i)
     kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0);        // dvp^T: (v, j)
-      mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0);  // scale qg^T do
+      mma3(tmem + 128 + 128 * (s / NSC), ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8,
+           s % NSC > 0);                                                         // scale qg^T do
     });
   }
   uint32_t ph = 0;
@@ -450,7 +454,8 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   // K = j) in shared memory, the B operand of -W^T dvp.
   float* dvp = ws.dvp + chunk * C * D;
   float* dt = sm;
-  float amax = 0.f;
+  float amax[2] = {0.f, 0.f};   // per reference chunk (column j's chunk)
+  const int R = C / p.sub;
   for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
     float* hi = dt + (c0 / KS) * 2 * SLICE_FLOATS;
 #pragma unroll
@@ -459,15 +464,17 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         y[t] = san(x[k + t], p.clip);
-        amax = fmaxf(amax, fabsf(y[t]));
+        amax[c0 >= R] = fmaxf(amax[c0 >= R], fabsf(y[t]));
         dvp[(c0 + k + t) * D + v] = y[t];
       }
       st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + k, KS, make_float4(y[0], y[1], y[2], y[3]));
     }
   });
   // max |dv_partial|: the constant part of the backward guard
-  amax = block_max(amax, ts.red);
-  if (threadIdx.x == 0) ws.bnd[chunk * 4 + 1] = amax;
+  for (int hf = 0; hf < p.sub; ++hf) {
+    const float m = block_max(amax[hf], ts.red);
+    if (threadIdx.x == 0) ws.bnd[(chunk * p.sub + hf) * 4 + 1] = m;
+  }
   const float* wt = ws.WT + chunk * C * D;
   ring.base = sm + 4 * 2 * SLICE_FLOATS;
   ring.nop = 1;
@@ -475,16 +482,20 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
     const Src srcs[1] = {direct(wt, C, -1.f)};   // (d,j) = -W
     kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       float* hi = dt + s * 2 * SLICE_FLOATS;
-      mma3(tmem + 128, ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128, KS / 8, 1);
+      mma3(tmem + 128 + 128 * (s / NSC), ring.op(buf, 0), kmajor(hi, hi + SLICE_FLOATS, KS), 128,
+           KS / 8, 1);
     });
   }
   drain(&ts.done, ph, ws.status);
-  float* eo = ws.E + chunk * D * D;
-  for_acc<128>(tmem, 128, [&](int d, int c0, const float* x) {
+#pragma unroll 1
+  for (int hf = 0; hf < p.sub; ++hf) {
+    float* eo = ws.E + (chunk * p.sub + hf) * D * D;
+    for_acc<128>(tmem, 128 + 128 * hf, [&](int d, int c0, const float* x) {
 #pragma unroll
-    for (int k = 0; k < 16; k += 4) st4f(eo + d * D + c0 + k, make_float4(x[k], x[k + 1], x[k + 2], x[k + 3]));
-  });
-  tc_teardown(tmem, 256);
+      for (int k = 0; k < 16; k += 4) st4f(eo + d * D + c0 + k, make_float4(x[k], x[k + 1], x[k + 2], x[k + 3]));
+    });
+  }
+  tc_teardown(tmem, 512);
 }
 
 
@@ -538,7 +549,16 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
   // The (b, h) whose guard failed rerun the reference's three-product step
   // (the CTAs of every other (b, h) return at once).
   hook.begin(kStageBwdExact, s);
-  if ((e = launch_bwd_state<C, D>(p, ws, dout, dh_final, dh0, s, true)) != cudaSuccess) return e;
+  if (p.sub == 1) {
+    if ((e = launch_bwd_state<C, D>(p, ws, dout, dh_final, dh0, s, true)) != cudaSuccess) return e;
+  } else {   // paired tiles: the 64-row step over the reference chunks
+    Problem p64 = p;
+    p64.C = C / 2;
+    p64.nc = p.ncs();
+    p64.sub = 1;
+    if ((e = launch_bwd_state<C / 2, D>(p64, ws, dout, dh_final, dh0, s, true, true)) != cudaSuccess)
+      return e;
+  }
   hook.end(kStageBwdExact, s);
   // dv_new is formed by the first product of k_tc_bwd_intra1
   return cudaSuccess;

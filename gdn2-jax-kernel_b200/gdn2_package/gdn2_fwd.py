@@ -36,6 +36,14 @@ CLIP = 1e4   # stage sanitiser bound
 # to float32 rounding unless a gate is positive and the +-20 exponent clip or
 # CLIP saturate (they act per chunk).
 EXACT_BT = True
+# BT = 64 with D = 128 (and T a multiple of 128) runs on the tensor-core
+# kernels, two chunks per 128-row tile computing the same BT = 64 function.
+# With a positive log-decay gate (outside -softplus's range; the reference
+# tests' all-ones inputs) the chunk states saturate at CLIP and some
+# gradients become cancellations of ~CLIP^2-sized products, where the
+# 3xTF32 products' relative error (~2^-22 of each term) shows: such calls,
+# and PAIR64 = False, run the float32 CUDA-core kernels instead.
+PAIR64 = True
 # T not a multiple of BT: the reference refuses it (gdn2_fwd.py:145-146), as
 # does this module by default.  MASKED_TAIL = True instead pads the sequence
 # with zero tokens (g = 0, k = q = v = w = b = 0), which leave the state and
@@ -166,6 +174,9 @@ class _Prepared:
         self.t = tuple(t.to(device=dev, dtype=cdt, non_blocking=True).contiguous() for t in ts)
         if T != self.T_user:
             self.t = tuple(self.pad(t) for t in self.t)
+        if self.C == 64 and D == 128 and T % 128 == 0:   # the paired tensor-core tiles apply
+            if not PAIR64 or (GATES == "activated" and bool((self.t[5] > 0).any())):
+                self.code |= _lib.NO_PAIR
         self.clip = float(CLIP)
         self.scale = float(scale)
         if h0 is None:
@@ -257,6 +268,7 @@ def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_t
     the batch-major (B, H, nc, ...) layout the backward consumes.  The
     reference additionally returns Akk, which the fused kernels never store."""
     p = _Prepared(q, k, v, w, b, g, scale, h0)
+    p.code |= _lib.NO_PAIR   # the residual views below follow the one-chunk tile layout
     o, h_final, ws = _run_forward(p, save_residuals=True, debug_tag=debug_tag)
     res = {n: t.clone() for n, t in _unpack_residuals(p, ws).items()}
     if p.on_host:

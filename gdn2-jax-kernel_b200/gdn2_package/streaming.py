@@ -124,8 +124,11 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
         raise _fwd.Gdn2ShapeError(f"heads={Hs} must divide the head count H={H}")
     dev = torch.device("cuda", torch.cuda.current_device())
     # constants and chunking are validated exactly as for the device path
-    p = _fwd._Prepared(*[torch.empty((Bs, T, Hs, D), dtype=dt, device=dev)] * 6, scale,
+    p = _fwd._Prepared(*[torch.zeros((Bs, T, Hs, D), dtype=dt, device=dev)] * 6, scale,
                        None if h0_h is None else torch.empty((Bs, Hs, D, D), device=dev))
+    if p.C == 64 and D == 128 and T % 128 == 0 and _fwd.GATES == "activated" and \
+            bool((xs[5] > 0).any()):
+        p.code |= _lib.NO_PAIR   # as _Prepared decides for device tensors
     lib = _lib.load()
     if out is None:
         pin = torch.cuda.is_available()

@@ -39,6 +39,11 @@ enum { GDN2_F32 = 0, GDN2_BF16 = 1 };
  * gdn2_bwd then returns dw, db, dg with respect to the pre-activations.  The
  * same flag must be given to the forward and the backward of one step. */
 #define GDN2_GATES_RAW 0x100
+/* OR-ed into the dtype argument of gdn2_fwd / gdn2_bwd / gdn2_fwd_noalloc:
+ * this call runs BT = 64 on the CUDA-core kernels even where
+ * gdn2_pair64_enable() would pair chunks on the tensor cores (the forward
+ * and the backward of one step must agree). */
+#define GDN2_NO_PAIR 0x200
 enum {
   GDN2_OK = 0,
   GDN2_ERR_INVALID = -1,   /* bad shape / argument (reference: AssertionError, gdn2_fwd.py:145-146) */
@@ -131,7 +136,8 @@ int gdn2_diag_enable(int on);
  * tile (block-diagonal chunk scores and WY solve, gates and gc_last per
  * chunk, one state step per chunk), the same function as the BT = 64
  * CUDA-core kernels.  Needs T % 128 == 0 (otherwise the CUDA-core kernels
- * run).  Returns the previous setting. */
+ * run).  On by default; per call, GDN2_NO_PAIR opts out.  Returns the
+ * previous setting. */
 int gdn2_pair64_enable(int on);
 int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
                    int* nonfinite, float* maxabs);

@@ -415,6 +415,7 @@ def test_stage_diagnostics_from_device_counters(BT, BC, monkeypatch, capsys):
     assert "t:kernel_A_Aqk" not in out and "non-finite" not in out, out
     from gdn2_package.gdn2_fwd import _Prepared, _run_forward
     p = _Prepared(*args, inp["scale"], torch.as_tensor(inp["h0"]).cuda())
+    p.code |= _lib.NO_PAIR   # the kernels gdn2_pallas_forward_with_residuals ran
     o2, h2, ws = _run_forward(p, save_residuals=True, debug_tag="t")
     stats = _lib.diag_read(ws, p.stream)
     for tag, t in (("kernel_C_u", res["u"]), ("kernel_D_o", o2), ("kernel_D_h_final", h2),
