@@ -196,8 +196,9 @@ def tensor_peak(cfg, bf16_tflops):
     dim = 128 kernels compute every product as 3xTF32 (three kind::tf32 MMAs
     per logical product; dense TF32 runs at half the bf16 rate), so their
     ceiling is bf16 / 2 / 3.  The 64-row kernels run on the CUDA cores: 148
-    SMs x 128 FMA/clk x 2 x 1.965 GHz."""
-    if cfg["BT"] == 128 and cfg["D"] == 128:
+    SMs x 128 FMA/clk x 2 x 1.965 GHz.  BT = 64 with D = 128 runs the
+    tensor-core kernels on tiles of two chunks (gdn2_fwd.PAIR64)."""
+    if cfg["D"] == 128 and (cfg["BT"] == 128 or (cfg["BT"] == 64 and cfg["T"] % 128 == 0)):
         return bf16_tflops / 6.0, "3xTF32 logical = measured bf16 burst / 2 (TF32) / 3"
     return 148 * 128 * 2 * 1.965e9 / 1e12, "fp32 CUDA-core FMA (148 SMs x 128 x 2 x 1.965 GHz)"
 

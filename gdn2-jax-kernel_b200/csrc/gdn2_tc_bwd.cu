@@ -628,6 +628,46 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   teardown(tmem);
 }
 
+// Statistics of the order-free B4 guard from one staged slice: fm holds
+// dM(i = d0 + comp, j = j0 + jj) (left passes: row and column L1 of dAqk in
+// pass 0, of dAkk in pass 1); fx the raw k (pass 0), q (pass 2) or k (pass 3,
+// fb its gate) at rows j0 + jj, columns d0 + comp: column maxima.  gst rows
+// as k_tc_bwd_intra3's enum.
+__device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Frag& fm,
+                                             const Frag& fx, const Frag& fb, float scale,
+                                             float* gst) {
+  auto amax = [](float* a, float v) {   // v >= 0 (or NaN, which the guard test rejects)
+    atomicMax(reinterpret_cast<int*>(a), __float_as_int(v));
+  };
+  if (pass < 2) {
+    float* rowl = gst + (pass == 0 ? 0 : 1) * 128;
+    float* coll = gst + (pass == 0 ? 2 : 3) * 128;
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = fm.v[j];
+      const float a = fabsf(v.x), b2 = fabsf(v.y), c2 = fabsf(v.z), d2 = fabsf(v.w);
+      r[0] += a; r[1] += b2; r[2] += c2; r[3] += d2;
+      atomicAdd(coll + j0 + j, a + b2 + c2 + d2);
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) atomicAdd(rowl + d0 + t, r[t]);
+  }
+  if (pass == 1) return;
+  float m[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float4 v = fx.v[j];
+    if (pass == 2) v = make_float4(scale * v.x, scale * v.y, scale * v.z, scale * v.w);
+    if (pass == 3) v = make_float4(fb.v[j].x * v.x, fb.v[j].y * v.y, fb.v[j].z * v.z, fb.v[j].w * v.w);
+    m[0] = fmaxf(m[0], fabsf(v.x)); m[1] = fmaxf(m[1], fabsf(v.y));
+    m[2] = fmaxf(m[2], fabsf(v.z)); m[3] = fmaxf(m[3], fabsf(v.w));
+  }
+  float* mx = gst + (pass == 0 ? 4 : (pass == 2 ? 5 : 6)) * 128;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) amax(mx + d0 + t, m[t]);
+}
+
 // ---------------------------------------------------------------------------
 // Backward of the chunk scores (B4, gdn2_bwd.py:248-339), the in-chunk
 // reverse cumsum (B5, gdn2_bwd.py:32-41) and the final assembly with the
@@ -649,6 +689,10 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
                 T* __restrict__ db_out, T* __restrict__ dg_out, Problem p, Workspace ws) {
   extern __shared__ __align__(128) float sm[];
   __shared__ __align__(16) TcSmemB ts;
+  // statistics of the order-free guard (BC < JW): row / column L1 of dAqk,
+  // dAkk; column maxima of |k|, |scale q|, |b k|
+  __shared__ float gstat[7][128];
+  enum { kRowQ = 0, kRowK, kColQ, kColK, kKmax, kLqmax, kLkmax };
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % p.nc);
   const size_t bh = chunk / p.nc;
@@ -694,11 +738,24 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     spread = fmaxf(spread, fabsf(gc[(32 * J) * GLD + d] - gc[(32 * J + 31) * GLD + d]));
     if (J < 2) spread64 = fmaxf(spread64, fabsf(gc[(64 * J) * GLD + d] - gc[(64 * J + 63) * GLD + d]));
   }
-  // The fast path's column blocks must nest inside the reference's BC-row
-  // sub-blocks for its clip guard (below) to hold, so BC < 32 takes the exact
-  // pair-ordered path.
-  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread || p.bc < 32;
+  const bool exact = gmax > 0.f || block_max(spread, red) > 80.f || spread != spread;
   const int JW = (block_max(spread64, red) <= 80.f && p.bc % 64 == 0) ? 64 : 32;
+  // The block guard below needs the JW-column blocks to nest inside the
+  // reference's BC-row sub-blocks.  For BC < JW the fast path is guarded
+  // instead by sums of absolute terms, which bound every prefix of the
+  // reference's pair sequence whatever its order (with g <= 0 every decay
+  // factor e^{gc_i - gc_j}, j <= i, is at most 1):
+  //   |dq|  <= |scale| rowL1(dAqk)_i kmax_d      |dbk| <= rowL1(dAkk)_i kmax_d
+  //   |dk|  <= colL1(dAqk)_j lqmax_d + colL1(dAkk)_j lkmax_d
+  //   |dgc| <= (lqmax rowL1(dAqk) + lkmax rowL1(dAkk)) kmax + kmax |dk bound|
+  // with kmax_d = max_i |k_id|, lqmax_d = max_i |scale q_id|,
+  // lkmax_d = max_i |b_i k_id| over the tile.  The staging gathers them.
+  const bool crude = p.bc < JW;
+  float* gst = &gstat[0][0];
+  if (crude) {
+    for (int e = threadIdx.x; e < 7 * 128; e += kThreads) gst[e] = 0.f;
+    __syncthreads();
+  }
   bool run_exact = exact;
   const int R = C / p.sub;   // rows of one reference chunk
   GDN2_TMARK(1);
@@ -764,6 +821,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           for (int j = 0; j < 4; ++j)
             fb.v[j] = ld4_gate<T>(bc + (k0 + kb * 4 + j) * rs + d0, GATES, kGateB);
         }
+        if (crude) gather_stats(pass, k0 + kb * 4, d0, fm, fx, fb, p.scale, gst);
         if (threadIdx.x == 0 && pend_buf >= 0) {
           mma3(tmem + 128 * pend_J, ring.op(pend_buf, 0), ring.op(pend_buf, 1), 128, KS / 8, pend_acc);
           commit(&ring.bars[pend_buf]);
@@ -930,8 +988,22 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     }
     const float lim = p.clip * (1.f - 1e-5f);   // NaN fails every test below
     GDN2_TMARK(9);
-    const bool bad = !(gq_dq < lim && gq_dbk < lim && gq_dk2 + gq_dk3 < lim &&
-                       gg0 + gg1 + gg2 + gg3 < lim);
+    bool bad;
+    if (!crude) {
+      bad = !(gq_dq < lim && gq_dbk < lim && gq_dk2 + gq_dk3 < lim && gg0 + gg1 + gg2 + gg3 < lim);
+    } else {
+      __syncthreads();   // the statistics of every thread are in
+      const float rq = gstat[kRowQ][x], rk = gstat[kRowK][x];
+      const float cq = gstat[kColQ][x], ck = gstat[kColK][x];
+      bad = false;
+#pragma unroll 4
+      for (int d = cb; d < cb + 64; ++d) {
+        const float km = gstat[kKmax][d], lq = gstat[kLqmax][d], lk = gstat[kLkmax][d];
+        const float bdk = cq * lq + ck * lk;
+        const float bdg = (lq * rq + lk * rk) * km + km * bdk;
+        bad |= !(fabsf(p.scale) * rq * km < lim && rk * km < lim && bdk < lim && bdg < lim);
+      }
+    }
     run_exact = __syncthreads_or(bad);
     // dgc total into shared memory (ring is idle after the last drain)
     if (!run_exact) {

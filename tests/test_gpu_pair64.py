@@ -176,15 +176,18 @@ def test_positive_gates_take_the_float32_kernels(paired):
     assert torch.equal(o, o2) and torch.equal(h, h2)
 
 
+@pytest.mark.parametrize("BC", [16, 32])
 @pytest.mark.parametrize("clip,dscale,h0s,gscale", [
     (20.0, 30.0, 0.1, 1.0),    # dv_new clips in the backward chain: exact recompute
     (0.3, 1.0, 0.1, 1.0),      # U, W, kg, o and the backward clip
     (0.5, 1.0, 0.1, 0.01),     # the forward state clips between the chunks of a tile
 ])
-def test_backward_with_clip_active(paired, clip, dscale, h0s, gscale, monkeypatch):
+def test_backward_with_clip_active(paired, clip, dscale, h0s, gscale, BC, monkeypatch):
+    """BC = 16 is guarded by the order-free bound of the B4 accumulators,
+    BC = 32 by the block partials."""
     from gdn2_package import gdn2_backward
     monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
-    _set(64, 32, clip)
+    _set(64, BC, clip)
     inp = make_inputs(2, 768, 2, 128, seed=31, h0_std=h0s)
     inp["g"] = inp["g"] * np.float32(gscale)
     inp["dout"] = inp["dout"] * np.float32(dscale)
@@ -195,7 +198,7 @@ def test_backward_with_clip_active(paired, clip, dscale, h0s, gscale, monkeypatc
                           torch.as_tensor(inp["dh_final"]).cuda())
     assert _lib.LAST_STATUS & _lib.STATUS_EXACT_RECOMPUTE, _lib.LAST_STATUS
     g_r = O.backward(*[inp[n].astype(np.float64) for n in NAMES], inp["scale"], inp["h0"],
-                     inp["dout"], inp["dh_final"], 64, 32, clip)
+                     inp["dout"], inp["dh_final"], 64, BC, clip)
     for name, a, b in zip(GRADS, grads, g_r):
         assert rel(a, b) < 1e-4, (name, rel(a, b))
 
@@ -215,3 +218,25 @@ def test_trainable_keeps_residuals(paired):
     direct = gdn2_backward(*[a.detach() for a in args], inp["scale"], h0.detach(), do, dhf)
     for name, a, b in zip(GRADS, [*[a.grad for a in args], h0.grad], direct):
         assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("BT", [64, 128])
+def test_b4_order_free_guard_bc16(paired, BT, monkeypatch):
+    """BC = 16 below the score kernel's 32-column blocks: with nothing near
+    CLIP the fast path runs (no B4 exact status) and matches the oracle; with
+    CLIP small the guard sends the tiles to the pair-ordered path."""
+    from gdn2_package import gdn2_backward
+    monkeypatch.setattr(_lib, "CHECK_STATUS", "always")
+    for clip in (1e4, 2.0):
+        _set(BT, 16, clip)
+        inp = make_inputs(1, 512, 2, 128, seed=41, h0_std=0.1)
+        args = [torch.as_tensor(inp[n]).cuda() for n in NAMES]
+        h0 = torch.as_tensor(inp["h0"]).cuda()
+        grads = gdn2_backward(*args, inp["scale"], h0, torch.as_tensor(inp["dout"]).cuda(),
+                              torch.as_tensor(inp["dh_final"]).cuda())
+        exact_b4 = bool(_lib.LAST_STATUS & _lib.STATUS_B4_EXACT)
+        assert exact_b4 == (clip < 1e4), (clip, _lib.LAST_STATUS)
+        g_r = O.backward(*[inp[n].astype(np.float64) for n in NAMES], inp["scale"], inp["h0"],
+                         inp["dout"], inp["dh_final"], BT, 16, clip)
+        for name, a, b in zip(GRADS, grads, g_r):
+            assert rel(a, b) < 1e-4, (clip, name, rel(a, b))

@@ -57,6 +57,7 @@ def test_bench_tables_cover_every_profiled_stage():
     f, b = bench.step_work(bench.CONFIGS[1])
     assert abs(f - 2.19e11) / 2.19e11 < 0.01 and abs(b - 4.03e9) / 4.03e9 < 0.01
     assert bench.tensor_peak(bench.CONFIGS[1], 1659.4)[0] == 1659.4 / 6
+    assert bench.tensor_peak(bench.CONFIGS[2], 1659.4)[0] == 1659.4 / 6   # paired BT = 64 tiles
     assert bench._shard(bench.CONFIGS[1], 8, 0, "strong") == (1, 6)
     assert bench._shard(bench.CONFIGS[1], 4, 0, "strong") == (2, 6)
     assert bench._shard(bench.CONFIGS[1], 8, 0, "weak") == (8, 6)
