@@ -306,7 +306,7 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
     const float dclip = (hf == 1 && last_tile) ? p.clip : 0.f;
     const Src srcs[2] = {rows(direct(ws.kg + chunk * C * D, D), hf * R, hf * R + R),
                          trans(dhn[hf], D, 1.f, dclip)};   // (i,d), (v,d)
-    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false, 4, true>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0 || hf > 0);
     });
   }
@@ -335,7 +335,7 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
   for (int hf = 0; hf < 2; ++hf) {
     const Src srcs[3] = {rows(direct(doc, rs), hf * R, hf * R + R), direct(hp[hf], D),
                          rows(direct(dv, D, -1.f), hf * R, hf * R + R)};   // (i,v) (dk,v) (i,v)
-    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false, 4, true>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 0), ring.op(buf, 1), 128, KS / 8, s > 0 || hf > 0);
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);
     });
@@ -346,7 +346,7 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
   for (int hf = 0; hf < 2; ++hf) {
     const Src srcs[3] = {rows(direct(vnew, D), hf * R, hf * R + R), direct(doc, rs),
                          direct(dhn[hf], D)};   // (j,v) (i,v) (dk,v)
-    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    kloop_pf<false, 4, true>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
       mma3(tmem + 256, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);
       mma3(tmem + 384, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0 || hf > 0);
     });
@@ -617,10 +617,10 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   __syncthreads();
   // strictly lower and, for a tile of two chunks, block-diagonal (the 4
   // columns i of one store lie in one chunk)
-  const int R = C / p.sub;
+  const int cm = p.sub == 2 ? C / 2 : 0;   // chunk bit of a row index
   for_tile([&](int j, int i) {
     const float4 x = lds4(t0 + j * TLD + i);
-    const bool same = j / R == i / R;
+    const bool same = ((j ^ i) & cm) == 0;
     st4(dAkkT + j * C + i, same && j < i ? san(-x.x, p.clip) : 0.f,
         same && j < i + 1 ? san(-x.y, p.clip) : 0.f, same && j < i + 2 ? san(-x.z, p.clip) : 0.f,
         same && j < i + 3 ? san(-x.w, p.clip) : 0.f);
@@ -682,7 +682,7 @@ __device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Fra
 // is dgc_i += L_i dL_i, dgc_j -= k_j dR_j.  The dk and dgc partials stay in
 // registers (thread = TMEM row) across the passes.
 // ---------------------------------------------------------------------------
-template <typename T, bool GATES>
+template <typename T, bool GATES, bool CRUDE>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ b,
                 const T* __restrict__ g, T* __restrict__ dq_out, T* __restrict__ dk_out,
@@ -750,7 +750,9 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   //   |dgc| <= (lqmax rowL1(dAqk) + lkmax rowL1(dAkk)) kmax + kmax |dk bound|
   // with kmax_d = max_i |k_id|, lqmax_d = max_i |scale q_id|,
   // lkmax_d = max_i |b_i k_id| over the tile.  The staging gathers them.
-  const bool crude = p.bc < JW;
+  // (JW >= 32 always, and 64 only for BC a multiple of 64: BC < JW iff
+  // BC < 32, which the launch resolves into the CRUDE instance)
+  constexpr bool crude = CRUDE;
   float* gst = &gstat[0][0];
   if (crude) {
     for (int e = threadIdx.x; e < 7 * 128; e += kThreads) gst[e] = 0.f;
@@ -758,6 +760,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   bool run_exact = exact;
   const int R = C / p.sub;   // rows of one reference chunk
+  const int cm = p.sub == 2 ? C / 2 : 0;   // rows x, r share a chunk iff ((x ^ r) & cm) == 0
   GDN2_TMARK(1);
 
   if (!exact) {
@@ -888,7 +891,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           const int r = JW * J;
           // same chunk only (paired tiles): across chunks the gc are of
           // different chunks and the factor below is meaningless
-          const bool use = (left ? (x >= r) : (x < r + JW)) && x / R == r / R;
+          const bool use = (left ? (x >= r) : (x < r + JW)) && ((x ^ r) & cm) == 0;
           if (use) {
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
@@ -1052,7 +1055,8 @@ cudaError_t launch_tc_bwd_intra3(const T* q, const T* k, const T* b, const T* g,
                                  cudaStream_t s, const LaunchHook& hook) {
   // ring (also the C x D dgc tile at the end), then the gc tile
   constexpr size_t smem = 2 * 2 * (size_t)SLICE_BYTES + (size_t)C * (D + 4) * sizeof(float);
-  auto kern = p.gates ? k_tc_bwd_intra3<T, true> : k_tc_bwd_intra3<T, false>;
+  auto kern = p.bc < 32 ? (p.gates ? k_tc_bwd_intra3<T, true, true> : k_tc_bwd_intra3<T, false, true>)
+                        : (p.gates ? k_tc_bwd_intra3<T, true, false> : k_tc_bwd_intra3<T, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   hook.begin(kStageBwdIntra3, s);

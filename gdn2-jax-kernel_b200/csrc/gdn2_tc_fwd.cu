@@ -130,6 +130,9 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   // chunk-local gc: with two 64-row chunks per tile the cumsum restarts at row 64
   column_cumsum<C, D, GLD>(sgc, red, p.sub == 2);
   const int R = C / p.sub;   // rows of one reference chunk
+  // bit tests instead of divisions by R: rows i, j are in one chunk iff
+  // ((i ^ j) & cm) == 0, and i | lm is the last row of i's chunk
+  const int cm = p.sub == 2 ? 64 : 0, lm = R - 1;
   GDN2_TMARK(10);
   // largest decay-block width (64 or 32 rows) whose in-block gc spread keeps
   // every factor e^{gc_r - gc_j} inside the float range
@@ -164,7 +167,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       int i, d;
       kq_at(4 * bt + u, i, d);
       const float4 kv = kcur[u], qv = qcur[u];
-      const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(sgc + ((i / R) * R + R - 1) * GLD + d);
+      const float4 gi = lds4(sgc + i * GLD + d), l4 = lds4(sgc + (i | lm) * GLD + d);
       const float4 kg4 = make_float4(san(kv.x * __expf(l4.x - gi.x), p.clip),
                                      san(kv.y * __expf(l4.y - gi.y), p.clip),
                                      san(kv.z * __expf(l4.z - gi.z), p.clip),
@@ -272,7 +275,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
           float4 aq = make_float4(0.f, 0.f, 0.f, 0.f), ak = aq;
           // rows of the column block's own chunk only (block-diagonal when
           // the tile holds two chunks)
-          if (i >= r && i / R == r / R) {
+          if (i >= r && ((i ^ r) & cm) == 0) {
             const float4 gi = lds4(sgc + i * GLD + d), gr = lds4(sgc + r * GLD + d);
             const float e0 = __expf(gi.x - gr.x), e1 = __expf(gi.y - gr.y),
                         e2 = __expf(gi.z - gr.z), e3 = __expf(gi.w - gr.w);
@@ -310,7 +313,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     for_acc<128>(tmem, 0, [&](int i, int c, const float* v) {   // Aqk / scale
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        aqkT[(c + t) * C + i] = c + t <= i && (c + t) / R == i / R ? san(p.scale * v[t], p.clip) : 0.f;
+        aqkT[(c + t) * C + i] = c + t <= i && (((c + t) ^ i) & cm) == 0 ? san(p.scale * v[t], p.clip) : 0.f;
         if (DIAG) dsc.add(aqkT[(c + t) * C + i]);
       }
     });
@@ -318,7 +321,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     for_acc<128>(tmem, 128, [&](int i, int c, const float* v) {   // S[j][i] = Akk(i, j)
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        S[(c + t) * TLD + i] = c + t < i && (c + t) / R == i / R ? san(v[t], p.clip) : 0.f;
+        S[(c + t) * TLD + i] = c + t < i && (((c + t) ^ i) & cm) == 0 ? san(v[t], p.clip) : 0.f;
         if (DIAG) dsc.add(S[(c + t) * TLD + i]);
       }
     });
@@ -327,7 +330,7 @@ k_tc_fwd_intra(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     // exact elementwise form with the +-20 exponent clip (gdn2_fwd.py:124-139)
     for (int e = threadIdx.x; e < C * C; e += kThreads) {
       const int i = e % C, j = e / C;
-      const bool pair = j <= i && j / R == i / R;   // same chunk, causal
+      const bool pair = j <= i && ((j ^ i) & cm) == 0;   // same chunk, causal
       float sq = 0.f, sk = 0.f;
       if (pair) {
         for (int d = 0; d < D; ++d) {

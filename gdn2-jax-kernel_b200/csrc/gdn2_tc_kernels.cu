@@ -75,6 +75,7 @@ __device__ __forceinline__ void st4f(float* p, float4 v) { *reinterpret_cast<flo
 // ---------------------------------------------------------------------------
 // M = diag(e^{gc_last}) - kg^T W and Bc = kg^T U, one CTA per chunk.
 // ---------------------------------------------------------------------------
+template <int SUB>   // reference chunks per tile (p.sub)
 __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace ws) {
   extern __shared__ __align__(128) float sm[];
   __shared__ TcSmem ts;
@@ -88,9 +89,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
   uint32_t ph = 0;
   // one map per reference chunk: K = its rows (all 128, or 64 per chunk of a
   // paired tile)
-  const int R = C / p.sub;
+  constexpr int R = C / SUB;
 #pragma unroll 1
-  for (int hf = 0; hf < p.sub; ++hf) {
+  for (int hf = 0; hf < SUB; ++hf) {
     const int r0 = hf * R;
     const Src srcs[3] = {trans(kg + r0 * D, D), direct(wt + r0, C), trans(u + r0 * D, D)};   // (d,i)=kg, (d',i)=W, (v,i)=U
     auto issue = [&](int buf, int s) {
@@ -98,14 +99,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
       mma3(tmem + 128, ring.op(buf, 0), ring.op(buf, 2), 128, KS / 8, s > 0);   // kg^T U
       mma3(tmem + 256, ring.op(buf, 1), ring.op(buf, 0), 128, KS / 8, s > 0);   // (kg^T W)^T
     };
-    if (p.sub == 1) kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, issue);
-    else kloop_pf<false, 2>(ring, g, ws.status, srcs, NoExtra{}, issue);
+    kloop_pf<false, 4 / SUB>(ring, g, ws.status, srcs, NoExtra{}, issue);
     drain(&ts.done, ph, ws.status);
     // M and M^T leave TMEM row by row as the canonical K-slices the scan
     // streams with bulk copies (row = TMEM lane, K = column); the scan forms
     // the lo planes itself (the tensor core reads a float32 word as its tf32
     // head).
-    const size_t sc = chunk * p.sub + hf;   // reference chunk
+    const size_t sc = chunk * SUB + hf;   // reference chunk
     float* bo = ws.Bc + sc * D * D;
     const float* gl = ws.gcl + sc * D;
 #pragma unroll 1
@@ -130,10 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
       for (int j = 0; j < 16; j += 4)
         st4f(bo + row * D + c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
     });
-    // every thread's TMEM reads are complete before the next chunk's MMAs
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
+    if (hf + 1 < SUB) {   // every thread's TMEM reads complete before the next chunk's MMAs
+      fence_before_sync();
+      __syncthreads();
+      fence_after_sync();
+    }
   }
   tc_teardown(tmem, 512);
 }
@@ -336,6 +337,7 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
 // Chunk outputs from the chunk-entry state h (gdn2_fwd.py:349-359):
 //   vnew = U - W h  (-> ws.vnew),   o = san(scale qg h + Aqk vnew)  (-> o)
 // ---------------------------------------------------------------------------
+template <int SUB>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   extern __shared__ __align__(128) float sm[];
@@ -351,17 +353,18 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   int g = 0;
   // one K loop per reference chunk of the tile, each with that chunk's entry
   // state and the other chunk's rows of W and qg masked (paired tiles)
-  const int R = C / p.sub;
+  constexpr int R = C / SUB;
 #pragma unroll 1
-  for (int hf = 0; hf < p.sub; ++hf) {
-    const float* hp = ws.hpre + (chunk * p.sub + hf) * D * D;
+  for (int hf = 0; hf < SUB; ++hf) {
+    const float* hp = ws.hpre + (chunk * SUB + hf) * D * D;
     const int lo = hf * R, hi = lo + R;
     const Src srcs[3] = {rows(trans(wt, C), lo, hi), rows(trans(qgt, C, p.scale), lo, hi),
                          trans(hp, D)};  // W, s qg, h^T
-    kloop_pf<false>(ring, g, ws.status, srcs, NoExtra{}, [&](int buf, int s) {
+    auto issue = [&](int buf, int s) {
       mma3(tmem, ring.op(buf, 2), ring.op(buf, 0), 128, KS / 8, s > 0 || hf > 0);        // (W h)^T: (v, i)
       mma3(tmem + 128, ring.op(buf, 1), ring.op(buf, 2), 128, KS / 8, s > 0 || hf > 0);  // scale qg h: (i, v)
-    });
+    };
+    kloop_pf<false, 4, (SUB > 1)>(ring, g, ws.status, srcs, NoExtra{}, issue);
   }
   uint32_t ph = 0;
   drain(&ts.done, ph, ws.status);
@@ -421,6 +424,7 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
 //   dv_partial = san(Aqk^T do)  (B2, gdn2_bwd.py:93)          -> ws.dvp
 //   E = scale qg^T do - W^T dv_partial                        -> ws.E
 // ---------------------------------------------------------------------------
+template <int SUB>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   extern __shared__ __align__(128) float sm[];
@@ -429,10 +433,11 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   const int c = (int)(chunk % p.nc);
   const size_t bh = chunk / p.nc;
   const int h = (int)(bh % p.H), bb = (int)(bh / p.H);
-  const uint32_t tmem = tc_setup(&ts, 512);
+  constexpr uint32_t kCols = SUB == 1 ? 256 : 512;
+  const uint32_t tmem = tc_setup(&ts, kCols);
   // E of reference chunk hf accumulates at TMEM 128 + 128 hf; its K rows are
   // the slices [hf * NSC, (hf + 1) * NSC)
-  const int NSC = 4 / p.sub;
+  constexpr int NSC = 4 / SUB;
   Ring ring = make_ring(sm, &ts, 3);
   const long rs = p.row_stride();
   const float* doc = dout + ((long)bb * p.T + (long)c * C) * rs + (long)h * D;
@@ -454,8 +459,8 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   // K = j) in shared memory, the B operand of -W^T dvp.
   float* dvp = ws.dvp + chunk * C * D;
   float* dt = sm;
-  float amax[2] = {0.f, 0.f};   // per reference chunk (column j's chunk)
-  const int R = C / p.sub;
+  float amax0 = 0.f, amax1 = 0.f;   // per reference chunk (column j's chunk)
+  constexpr int R = C / SUB;
   for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
     float* hi = dt + (c0 / KS) * 2 * SLICE_FLOATS;
 #pragma unroll
@@ -464,16 +469,17 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         y[t] = san(x[k + t], p.clip);
-        amax[c0 >= R] = fmaxf(amax[c0 >= R], fabsf(y[t]));
+        if (SUB == 1 || c0 < R) amax0 = fmaxf(amax0, fabsf(y[t]));
+        else amax1 = fmaxf(amax1, fabsf(y[t]));
         dvp[(c0 + k + t) * D + v] = y[t];
       }
       st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + k, KS, make_float4(y[0], y[1], y[2], y[3]));
     }
   });
   // max |dv_partial|: the constant part of the backward guard
-  for (int hf = 0; hf < p.sub; ++hf) {
-    const float m = block_max(amax[hf], ts.red);
-    if (threadIdx.x == 0) ws.bnd[(chunk * p.sub + hf) * 4 + 1] = m;
+  for (int hf = 0; hf < SUB; ++hf) {
+    const float m = block_max(hf ? amax1 : amax0, ts.red);
+    if (threadIdx.x == 0) ws.bnd[(chunk * SUB + hf) * 4 + 1] = m;
   }
   const float* wt = ws.WT + chunk * C * D;
   ring.base = sm + 4 * 2 * SLICE_FLOATS;
@@ -488,14 +494,14 @@ k_tc_bwd_prep(Problem p, Workspace ws, const float* __restrict__ dout) {
   }
   drain(&ts.done, ph, ws.status);
 #pragma unroll 1
-  for (int hf = 0; hf < p.sub; ++hf) {
-    float* eo = ws.E + (chunk * p.sub + hf) * D * D;
+  for (int hf = 0; hf < SUB; ++hf) {
+    float* eo = ws.E + (chunk * SUB + hf) * D * D;
     for_acc<128>(tmem, 128 + 128 * hf, [&](int d, int c0, const float* x) {
 #pragma unroll
       for (int k = 0; k < 16; k += 4) st4f(eo + d * D + c0 + k, make_float4(x[k], x[k + 1], x[k + 2], x[k + 3]));
     });
   }
-  tc_teardown(tmem, 512);
+  tc_teardown(tmem, kCols);
 }
 
 
@@ -513,11 +519,13 @@ cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0
                           float* hfinal, cudaStream_t s, const LaunchHook& hook) {
   cudaError_t e;
   const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
-  if ((e = prep(k_tc_affine, kRing3)) != cudaSuccess) return e;
+  auto affine = p.sub == 2 ? k_tc_affine<2> : k_tc_affine<1>;
+  auto fwd_out = p.sub == 2 ? k_tc_fwd_out<2> : k_tc_fwd_out<1>;
+  if ((e = prep(affine, kRing3)) != cudaSuccess) return e;
   if ((e = prep(k_tc_scan<false>, kScan)) != cudaSuccess) return e;
-  if ((e = prep(k_tc_fwd_out, kRing3)) != cudaSuccess) return e;
+  if ((e = prep(fwd_out, kRing3)) != cudaSuccess) return e;
   hook.begin(kStageFwdAffine, s);
-  k_tc_affine<<<nchunks, kThreads, kRing3, s>>>(p, ws);
+  affine<<<nchunks, kThreads, kRing3, s>>>(p, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageFwdAffine, s);
   hook.begin(kStageFwdScan, s);
@@ -525,7 +533,7 @@ cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageFwdScan, s);
   hook.begin(kStageFwdOut, s);
-  k_tc_fwd_out<<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
+  fwd_out<<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageFwdOut, s);
   return cudaSuccess;
@@ -536,10 +544,11 @@ cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const flo
                                 const LaunchHook& hook) {
   cudaError_t e;
   const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
-  if ((e = prep(k_tc_bwd_prep, kRing3)) != cudaSuccess) return e;
+  auto bwd_prep = p.sub == 2 ? k_tc_bwd_prep<2> : k_tc_bwd_prep<1>;
+  if ((e = prep(bwd_prep, kRing3)) != cudaSuccess) return e;
   if ((e = prep(k_tc_scan<true>, kScan)) != cudaSuccess) return e;
   hook.begin(kStageBwdPrep, s);
-  k_tc_bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, dout);
+  bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, dout);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageBwdPrep, s);
   hook.begin(kStageBwdScan, s);
@@ -578,21 +587,21 @@ cudaError_t launch_tc_sp(int op, const Problem& p, const Workspace& ws, const fl
   }
   if (op == 1) {            // rescan from a given start state + chunk outputs
     if ((e = prep(k_tc_scan<false>, kScan)) != cudaSuccess) return e;
-    if ((e = prep(k_tc_fwd_out, kRing3)) != cudaSuccess) return e;
+    if ((e = prep(k_tc_fwd_out<1>, kRing3)) != cudaSuccess) return e;
     hook.begin(kStageFwdScan, s);
     k_tc_scan<false><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, in, out);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     hook.end(kStageFwdScan, s);
     hook.begin(kStageFwdOut, s);
-    k_tc_fwd_out<<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
+    k_tc_fwd_out<1><<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     hook.end(kStageFwdOut, s);
     return cudaSuccess;
   }
   // op == 2: backward segment term, zero incoming gradient
-  if ((e = prep(k_tc_bwd_prep, kRing3)) != cudaSuccess) return e;
+  if ((e = prep(k_tc_bwd_prep<1>, kRing3)) != cudaSuccess) return e;
   if ((e = prep(k_tc_scan<true>, kScan)) != cudaSuccess) return e;
-  k_tc_bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, in);
+  k_tc_bwd_prep<1><<<nchunks, kThreads, kRing3, s>>>(p, ws, in);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   k_tc_scan<true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, nullptr, out);
   return cudaGetLastError();

@@ -212,8 +212,11 @@ __device__ __forceinline__ Src rows(Src s, int lo, int hi) {
   s.rhi = hi;
   return s;
 }
+// MASK = false: the row range is ignored (every source of the one-chunk
+// kernels); MASK = true honours it.
+template <bool MASK = false>
 __device__ __forceinline__ void src_load(const Src& s, int k0, Frag& f) {
-  if (s.rlo == 0 && s.rhi == 128) {
+  if (!MASK) {
     if (s.trans) load_trans(f, s.p, s.ld, k0);
     else load_direct(f, s.p, s.ld, k0);
     return;
@@ -260,19 +263,19 @@ __device__ __forceinline__ void src_store(const Src& s, float* hi, float* lo, co
 // The slice loop is rolled (one copy of its body: the kernels run each K loop
 // once per chunk, so unrolled copies cost instruction-cache misses); the
 // register double buffer advances by copying the prefetched slice.
-template <int NS, int NOP, class Ex, class Is>
+template <int NS, bool MASK, int NOP, class Ex, class Is>
 __device__ __forceinline__ void kloop_pf_unrolled(Ring& ring, int& g, int* err,
                                                   const Src (&src)[NOP], Ex extra, Is issue) {
   Frag fa[NOP], fb[NOP];
 #pragma unroll
-  for (int o = 0; o < NOP; ++o) src_load(src[o], 0, fa[o]);
+  for (int o = 0; o < NOP; ++o) src_load<MASK>(src[o], 0, fa[o]);
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
     Frag* cur = (s & 1) ? fb : fa;
     Frag* nxt = (s & 1) ? fa : fb;
     if (s + 1 < NS) {
 #pragma unroll
-      for (int o = 0; o < NOP; ++o) src_load(src[o], (s + 1) * KS, nxt[o]);
+      for (int o = 0; o < NOP; ++o) src_load<MASK>(src[o], (s + 1) * KS, nxt[o]);
     }
     const int buf = g & 1;
     ring_acquire(ring, buf, g >> 1, err);
@@ -291,13 +294,14 @@ __device__ __forceinline__ void kloop_pf_unrolled(Ring& ring, int& g, int* err,
 // ROLL = false: the slice loop fully unrolled (measured faster for the short
 // kernels whose K loops carry few operands: affine, fwd_out, bwd_prep, and the
 // dv / dqg loops of bwd_intra1).  NS: 32-wide K slices (4 = K of 128; 2 = one
-// 64-row chunk of a paired tile, unrolled form only).
-template <bool ROLL = true, int NS = 128 / KS, int NOP, class Ex, class Is>
+// 64-row chunk of a paired tile), MASK: honour the sources' row ranges (both
+// unrolled form only).
+template <bool ROLL = true, int NS = 128 / KS, bool MASK = false, int NOP, class Ex, class Is>
 __device__ __forceinline__ void kloop_pf(Ring& ring, int& g, int* err, const Src (&src)[NOP],
                                          Ex extra, Is issue) {
-  static_assert(NS == 128 / KS || !ROLL, "partial K loops are unrolled");
+  static_assert((NS == 128 / KS && !MASK) || !ROLL, "partial or masked K loops are unrolled");
   if (!ROLL) {
-    kloop_pf_unrolled<NS>(ring, g, err, src, extra, issue);
+    kloop_pf_unrolled<NS, MASK>(ring, g, err, src, extra, issue);
     return;
   }
   Frag cur[NOP], nxt[NOP];
