@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "gdn2_package", "libgdn2.so")
-SOURCES = ["gdn2_fwd.cu", "gdn2_bwd.cu", "gdn2_capi.cu", "gdn2_selftest.cu", "gdn2_noalloc.cu", "gdn2_tc_kernels.cu", "gdn2_tc_bwd.cu", "gdn2_tc_fwd.cu", "gdn2_decode.cu"]
+SOURCES = ["gdn2_fwd.cu", "gdn2_bwd.cu", "gdn2_capi.cu", "gdn2_selftest.cu", "gdn2_noalloc.cu", "gdn2_tc_kernels.cu", "gdn2_tc_bwd.cu", "gdn2_tc_fwd.cu", "gdn2_decode.cu", "gdn2_stages.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo",
               "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

@@ -25,14 +25,17 @@ constexpr float kB4FinalClip = 1e4f;   // gdn2_pipeline.py:34
 // (i, j) at j * C + i.  pd*: the sanitised B3 partials of this chunk
 // ([C][D]).  Writes dq, dk, db (with the final +-1e4 sanitiser) and
 // sdg[x * D + d] = pdgc + clip(dgc) (the input of the B5 reverse cumsum).
-template <typename T>
+template <typename T, typename TO = T>   // input / output element types
 __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
                                const T* __restrict__ kc, const T* __restrict__ bc, long rs,
                                const float* gc, int gld, const float* __restrict__ dAqkT,
                                const float* __restrict__ dAkkT, const float* pdq, const float* pdk,
-                               const float* pdb, const float* pdgc, T* dq_out, T* dk_out,
-                               T* db_out, long off, float* sdg, float scale, float clip,
-                               int gates, int span) {
+                               const float* pdb, const float* pdgc, TO* dq_out, TO* dk_out,
+                               TO* db_out, long off, float* sdg, float scale, float clip,
+                               int gates, int span, long ors = -1,
+                               float final_clip = kB4FinalClip) {
+  // ors: row stride of the outputs (default: rs, the inputs' layout)
+  if (ors < 0) ors = rs;
   // span: rows of one reference chunk (C, or C / 2 for a tile of two chunks);
   // the pairs stay inside the chunk of row x
   const int nsc = span / BC;
@@ -88,11 +91,11 @@ __device__ void b4_exact_chunk(int C, int D, int BC, const T* __restrict__ qc,
     }
     // _kernel_b4_body's final sanitisers, then the pipeline's sum with B3
     // and the +-1e4 clip (gdn2_bwd.py:333-336, gdn2_pipeline.py:117-135)
-    const long o = off + x * rs + d;
-    dq_out[o] = from_f<T>(san(pdq[e] + san(dq, clip), kB4FinalClip));
-    dk_out[o] = from_f<T>(san(pdk[e] + san(dk + dbk * bx, clip), kB4FinalClip));
-    const float dbo = san(pdb[e] + san(dbk * kx, clip), kB4FinalClip);
-    db_out[o] = from_f<T>(gates ? dbo * bx * (1.f - bx) : dbo);
+    const long o = off + x * ors + d;
+    dq_out[o] = from_f<TO>(san(pdq[e] + san(dq, clip), final_clip));
+    dk_out[o] = from_f<TO>(san(pdk[e] + san(dk + dbk * bx, clip), final_clip));
+    const float dbo = san(pdb[e] + san(dbk * kx, clip), final_clip);
+    db_out[o] = from_f<TO>(gates ? dbo * bx * (1.f - bx) : dbo);
     sdg[e] = pdgc[e] + san(dgc, clip);
   }
 }

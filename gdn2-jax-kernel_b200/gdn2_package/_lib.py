@@ -45,6 +45,15 @@ SIGNATURES = {
     "gdn2_selftest_wait_timeout": (_i, [_vp, _sz, _i, _vp]),
     "gdn2_diag_enable": (_i, [_i]),
     "gdn2_pair64_enable": (_i, [_i]),
+    "gdn2_stage_scores": (_i, [_i] + [_vp] * 6 + [_i] * 5 + [_f, _f, _vp]),
+    "gdn2_stage_wy_solve": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),
+    "gdn2_stage_recompute_wy": (_i, [_i] + [_vp] * 12 + [_i] * 5 + [_f, _vp]),
+    "gdn2_stage_combine": (_i, [_vp] * 11 + [_i] * 5 + [_f, _f, _vp]),
+    "gdn2_stage_dhu": (_i, [_vp] * 10 + [_i] * 5 + [_f, _f, _vp]),
+    "gdn2_stage_dav": (_i, [_vp] * 5 + [_i] * 3 + [_f, _vp]),
+    "gdn2_stage_wy_dqkg": (_i, [_vp] * 20 + [_i] * 3 + [_f, _f, _vp]),
+    "gdn2_stage_intra_bwd": (_i, [_i] + [_vp] * 11 + [_i] * 6 + [_f, _f, _vp]),
+    "gdn2_stage_revcumsum": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),
     "gdn2_diag_read": (_i, [_vp, _sz, _vp, _i, ctypes.POINTER(ctypes.c_int),
                             ctypes.POINTER(ctypes.c_float)]),
 }

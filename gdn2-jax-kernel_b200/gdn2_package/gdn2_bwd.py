@@ -56,3 +56,102 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
         out = [t.cpu() for t in out]
         dh0 = dh0.cpu()
     return (*out, dh0)
+
+
+# ---------- the reference's stage functions (B1-B5, gdn2_bwd.py:32-375) ----------
+# Separate entry points on the reference's chunked layouts (one CUDA kernel
+# of libgdn2.so each, gdn2_stage_*); gdn2_backward above does not use them.
+
+def _dev_of(t):
+    t = torch.as_tensor(t)
+    return t.device if t.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+
+
+def reverse_cumsum_bwd(dgc, chunk_size):
+    """B5: dg_raw[i] = san(sum_{j >= i} dgc[j]) within each chunk of
+    ``chunk_size`` rows (gdn2_bwd.py:32-41); dgc is (..., chunk_size, D)."""
+    dev = _dev_of(dgc)
+    x = _fwd._f32(dgc, dev)
+    C, D = x.shape[-2], x.shape[-1]
+    if C != int(chunk_size):
+        raise _fwd.Gdn2ShapeError(f"dgc's chunk axis is {C}, chunk_size={chunk_size}")
+    out = torch.empty_like(x)
+    rc = _lib.load().gdn2_stage_revcumsum(x.data_ptr(), out.data_ptr(), x.numel() // (C * D), C, D,
+                                          float(_fwd.CLIP), _fwd._stream(dev))
+    _lib.check(rc, "reverse_cumsum_bwd")
+    return out
+
+
+def gdn2_dhu_backward(do, dv_partial, w_pseudo, qg, kg, gc_last, scale, dht=None):
+    """B1: dh_all (B, H, nc, D, D), dh0 (B, H, D, D), dv_all (B, H, nc, BT, D)
+    (gdn2_bwd.py:45-80); do is chunked (B, H, nc, BT, D)."""
+    dev = _dev_of(qg)
+    xs = [_fwd._f32(t, dev) for t in (do, dv_partial, w_pseudo, qg, kg, gc_last)]
+    B, H, nc, bt, D = xs[3].shape
+    dht = None if dht is None else _fwd._f32(dht, dev)
+    dh_all = torch.empty((B, H, nc, D, D), dtype=torch.float32, device=dev)
+    dh0 = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+    dv_all = torch.empty((B, H, nc, bt, D), dtype=torch.float32, device=dev)
+    rc = _lib.load().gdn2_stage_dhu(*[t.data_ptr() for t in xs],
+                                    dht.data_ptr() if dht is not None else None,
+                                    dh_all.data_ptr(), dh0.data_ptr(), dv_all.data_ptr(), B, H, nc,
+                                    bt, D, float(scale), float(_fwd.CLIP), _fwd._stream(dev))
+    _lib.check(rc, "gdn2_dhu_backward")
+    return dh_all, dh0, dv_all
+
+
+def dav_backward_pallas(Aqk, v_new, do):
+    """B2: dAqk = san((do v_new^T) * causal), dv_new = san(Aqk^T do)
+    (gdn2_bwd.py:84-122); all (B, H, nc, ., .)."""
+    dev = _dev_of(v_new)
+    aqk, vn, d = (_fwd._f32(t, dev) for t in (Aqk, v_new, do))
+    B, H, nc, bt, D = vn.shape
+    daqk = torch.empty_like(aqk)
+    dv = torch.empty_like(vn)
+    rc = _lib.load().gdn2_stage_dav(aqk.data_ptr(), vn.data_ptr(), d.data_ptr(), daqk.data_ptr(),
+                                    dv.data_ptr(), B * H * nc, bt, D, float(_fwd.CLIP),
+                                    _fwd._stream(dev))
+    _lib.check(rc, "dav_backward_pallas")
+    return daqk, dv
+
+
+def wy_dqkg_backward_pallas(q, k, b, w, v, gc, A, Akk, h_pre_all, v_new_all, do, dv, dh_next_all,
+                            scale):
+    """B3: dict of dq, dk, db, dw, dv_raw, dgc (B, H, nc, BT, D) and dAkk
+    (B, H, nc, BT, BT) (gdn2_bwd.py:126-244).  Every argument is chunked
+    batch-major; Akk is not read (as in the reference)."""
+    del Akk
+    dev = _dev_of(q)
+    xs = [_fwd._f32(t, dev) for t in (q, k, b, w, v, gc, A, h_pre_all, v_new_all, do, dv,
+                                      dh_next_all)]
+    B, H, nc, bt, D = xs[0].shape
+    outs = [torch.empty((B, H, nc, bt, D), dtype=torch.float32, device=dev) for _ in range(6)]
+    dakk = torch.empty((B, H, nc, bt, bt), dtype=torch.float32, device=dev)
+    scratch = torch.empty_like(dakk)
+    rc = _lib.load().gdn2_stage_wy_dqkg(*[t.data_ptr() for t in xs],
+                                        *[t.data_ptr() for t in outs], dakk.data_ptr(),
+                                        scratch.data_ptr(), B * H * nc, bt, D, float(scale),
+                                        float(_fwd.CLIP), _fwd._stream(dev))
+    _lib.check(rc, "wy_dqkg_backward_pallas")
+    dq, dk, db, dw, dv_raw, dgc = outs
+    return dict(dq=dq, dk=dk, db=db, dw=dw, dv_raw=dv_raw, dgc=dgc, dAkk=dakk)
+
+
+def intra_backward_pallas(dAqk, dAkk, q, k, b, g, scale):
+    """B4: dq, dk, db, dgc (B, H, nc, BT, D) from the score gradients, in the
+    reference's sub-block pair order with its clipped accumulation
+    (gdn2_bwd.py:248-375); q, k, b, g are (B, L, H, D)."""
+    B, L, H, D, bt = _fwd._check_seq(torch.as_tensor(q))
+    (q, k, b, g), code, dev = _fwd._stage_in((q, k, b, g))
+    tr = lambda t: _fwd._f32(t, dev).transpose(-1, -2).contiguous()
+    daqkT, dakkT = tr(dAqk), tr(dAkk)
+    nc = L // bt
+    outs = [torch.empty((B, H, nc, bt, D), dtype=torch.float32, device=dev) for _ in range(4)]
+    zeros = torch.zeros((bt, D), dtype=torch.float32, device=dev)
+    rc = _lib.load().gdn2_stage_intra_bwd(code, daqkT.data_ptr(), dakkT.data_ptr(), q.data_ptr(),
+                                          k.data_ptr(), b.data_ptr(), g.data_ptr(),
+                                          zeros.data_ptr(), *[t.data_ptr() for t in outs], B, L, H,
+                                          D, bt, int(_fwd.BC), float(scale), float(_fwd.CLIP),
+                                          _fwd._stream(dev))
+    _lib.check(rc, "intra_backward_pallas")
+    return tuple(outs)

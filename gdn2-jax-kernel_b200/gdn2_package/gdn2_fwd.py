@@ -274,3 +274,131 @@ def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_t
     if p.on_host:
         return o.cpu(), h_final.cpu(), {n: t.cpu() for n, t in res.items()}
     return o, h_final, res
+
+
+# ---------- the reference's stage functions (Kernels A-D, gdn2_fwd.py:142-397) ----------
+# Separate entry points on the reference's chunked layouts, for code that
+# composes the stages itself (gdn2_pipeline.py:14-31 imports them).  Each runs
+# one CUDA kernel of libgdn2.so (gdn2_stage_*); the fused forward above does
+# not use them.  BT, BC, CLIP are read at call time; BT is 64 or 128.
+
+def _stage_bt():
+    bt = int(BT)
+    if bt not in (64, 128):
+        raise Gdn2ShapeError(f"the stage functions run BT = 64 or 128; got BT={bt}")
+    return bt
+
+
+def _stage_in(ts):
+    """Device, common compute dtype (float32 or bfloat16) and the C code."""
+    ts = [torch.as_tensor(t) for t in ts]
+    dev = next((t.device for t in ts if t.device.type == "cuda"),
+               torch.device("cuda", torch.cuda.current_device()))
+    cdt = torch.bfloat16 if all(t.dtype == torch.bfloat16 for t in ts) else torch.float32
+    out = [t.to(device=dev, dtype=cdt).contiguous() for t in ts]
+    return out, (_lib.BF16 if cdt == torch.bfloat16 else _lib.F32), dev
+
+
+def _f32(t, dev):
+    return torch.as_tensor(t).to(device=dev, dtype=torch.float32).contiguous()
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check_seq(q):
+    B, L, H, D = q.shape
+    if D not in _SUPPORTED_D:
+        raise Gdn2ShapeError(f"head dim D={D} unsupported (64 or 128)")
+    bt = _stage_bt()
+    if L % bt:
+        raise Gdn2ShapeError(f"L={L} must be divisible by BT={bt}.")
+    return B, L, H, D, bt
+
+
+def build_chunk_scores_pallas(q, k, b, g, scale):
+    """Kernel A: Aqk, Akk of shape (B, H, n_chunks, BT, BT) (gdn2_fwd.py:142-170)."""
+    B, L, H, D, bt = _check_seq(torch.as_tensor(q))
+    (q, k, b, g), code, dev = _stage_in((q, k, b, g))
+    nc = L // bt
+    aqk = torch.empty((B, H, nc, bt, bt), dtype=torch.float32, device=dev)
+    akk = torch.empty_like(aqk)
+    rc = _lib.load().gdn2_stage_scores(code, q.data_ptr(), k.data_ptr(), b.data_ptr(),
+                                       g.data_ptr(), aqk.data_ptr(), akk.data_ptr(), B, L, H, D,
+                                       bt, float(scale), float(CLIP), _stream(dev))
+    _lib.check(rc, "build_chunk_scores_pallas")
+    return aqk, akk
+
+
+def wy_solve_pallas(Akk):
+    """Kernel B: A = (I + Akk)^-1 per chunk (gdn2_fwd.py:246-260).  The
+    sub-block level is the reference's block substitution for any number of
+    BC sub-blocks (the reference hard-codes two)."""
+    bt = _stage_bt()
+    Akk = torch.as_tensor(Akk)
+    if tuple(Akk.shape[-2:]) != (bt, bt):
+        raise Gdn2ShapeError(f"Akk must end in (BT, BT) = {(bt, bt)}")
+    dev = Akk.device if Akk.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    akk = _f32(Akk, dev)
+    a = torch.empty_like(akk)
+    n = akk.numel() // (bt * bt)
+    rc = _lib.load().gdn2_stage_wy_solve(akk.data_ptr(), a.data_ptr(), n, bt, int(BC),
+                                         float(CLIP), _stream(dev))
+    _lib.check(rc, "wy_solve_pallas")
+    return a
+
+
+def recompute_wy_pallas(q, k, v, w, b, g, A):
+    """Kernel C: w_pseudo, u, kg, qg (B, H, nc, BT, D) and gc_last (B, H, nc, D)
+    (gdn2_fwd.py:298-330)."""
+    B, L, H, D, bt = _check_seq(torch.as_tensor(q))
+    (q, k, v, w, b, g), code, dev = _stage_in((q, k, v, w, b, g))
+    nc = L // bt
+    a = _f32(A, dev)
+    if tuple(a.shape) != (B, H, nc, bt, bt):
+        raise Gdn2ShapeError(f"A must be {(B, H, nc, bt, bt)}")
+    shp = (B, H, nc, bt, D)
+    wp, u, kg, qg = (torch.empty(shp, dtype=torch.float32, device=dev) for _ in range(4))
+    gcl = torch.empty((B, H, nc, D), dtype=torch.float32, device=dev)
+    rc = _lib.load().gdn2_stage_recompute_wy(
+        code, q.data_ptr(), k.data_ptr(), v.data_ptr(), w.data_ptr(), b.data_ptr(), g.data_ptr(),
+        a.data_ptr(), wp.data_ptr(), u.data_ptr(), kg.data_ptr(), qg.data_ptr(), gcl.data_ptr(),
+        B, L, H, D, bt, float(CLIP), _stream(dev))
+    _lib.check(rc, "recompute_wy_pallas")
+    return wp, u, kg, qg, gcl
+
+
+def _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, with_state, debug_tag):
+    wp = torch.as_tensor(w_pseudo)
+    dev = wp.device if wp.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    B, H, nc, bt, D = wp.shape
+    if D not in _SUPPORTED_D or bt not in (64, 128):
+        raise Gdn2ShapeError(f"unsupported chunk tiles {tuple(wp.shape)}")
+    xs = [_f32(t, dev) for t in (Aqk, w_pseudo, u, kg, qg, gc_last)]
+    h0 = None if h0 is None else _f32(h0, dev)
+    o = torch.empty((B, H, nc, bt, D), dtype=torch.float32, device=dev)
+    hf = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+    hpre = torch.empty((nc, B, H, D, D), dtype=torch.float32, device=dev) if with_state else None
+    vall = torch.empty((nc, B, H, bt, D), dtype=torch.float32, device=dev) if with_state else None
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    rc = _lib.load().gdn2_stage_combine(*[t.data_ptr() for t in xs], ptr(h0), o.data_ptr(),
+                                        hf.data_ptr(), ptr(hpre), ptr(vall), B, H, nc, bt, D,
+                                        float(scale), float(CLIP), _stream(dev))
+    _lib.check(rc, "gdn2_inter_chunk_combine")
+    _stage_diag(f"{debug_tag}:kernel_D_h_final", hf)
+    _stage_diag(f"{debug_tag}:kernel_D_o", o)
+    return (o, hf, hpre, vall) if with_state else (o, hf)
+
+
+def gdn2_inter_chunk_combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0=None, debug_tag=""):
+    """Kernel D: o (B, H, nc, BT, D) and h_final (gdn2_fwd.py:338-366)."""
+    return _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, False, debug_tag)
+
+
+def gdn2_inter_chunk_combine_with_state(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0=None,
+                                        debug_tag=""):
+    """Kernel D that also returns h_pre_all (nc, B, H, D, D) and v_new_all
+    (nc, B, H, BT, D), chunk-major as the reference's scan stacks them
+    (gdn2_fwd.py:369-397)."""
+    return _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, True, debug_tag)

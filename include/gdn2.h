@@ -172,6 +172,56 @@ int gdn2_noalloc_status(void* stream);
 int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, size_t head_bytes,
                     int to_device, void* stream);
 
+/* The reference's stage functions as separate entry points, on its chunked
+ * layouts: (B, H, nc, BT, .) float32 tiles, gc_last (B, H, nc, D), inputs
+ * q..g (B, T, H, D) of `dtype` where named.  The fused gdn2_fwd / gdn2_bwd
+ * never call them.  Each replaces the reference function of the same name:
+ *   gdn2_stage_scores        build_chunk_scores_pallas (gdn2_fwd.py:142-170)
+ *   gdn2_stage_wy_solve      wy_solve_pallas (gdn2_fwd.py:246-260), any BT/BC
+ *   gdn2_stage_recompute_wy  recompute_wy_pallas (gdn2_fwd.py:298-330)
+ *   gdn2_stage_combine       gdn2_inter_chunk_combine(_with_state)
+ *                            (gdn2_fwd.py:338-397); h_pre_all (nc,B,H,D,D) and
+ *                            v_new_all (nc,B,H,BT,D) chunk-major, may be NULL
+ *   gdn2_stage_dhu           gdn2_dhu_backward (gdn2_bwd.py:45-80)
+ *   gdn2_stage_dav           dav_backward_pallas (gdn2_bwd.py:84-122)
+ *   gdn2_stage_wy_dqkg       wy_dqkg_backward_pallas (gdn2_bwd.py:126-244);
+ *                            scratch: n_chunks * BT * BT floats
+ *   gdn2_stage_intra_bwd     intra_backward_pallas (gdn2_bwd.py:248-375);
+ *                            dAqk / dAkk given transposed per chunk, zeros:
+ *                            BT * D zero floats
+ *   gdn2_stage_revcumsum     reverse_cumsum_bwd (gdn2_bwd.py:32-41) */
+int gdn2_stage_scores(int dtype, const void* q, const void* k, const void* b, const void* g,
+                      float* aqk, float* akk, int B, int T, int H, int D, int BT, float scale,
+                      float clip, void* stream);
+int gdn2_stage_wy_solve(const float* akk, float* a, int n_chunks, int BT, int BC, float clip,
+                        void* stream);
+int gdn2_stage_recompute_wy(int dtype, const void* q, const void* k, const void* v, const void* w,
+                            const void* b, const void* g, const float* a, float* w_pseudo,
+                            float* u, float* kg, float* qg, float* gc_last, int B, int T, int H,
+                            int D, int BT, float clip, void* stream);
+int gdn2_stage_combine(const float* aqk, const float* w_pseudo, const float* u, const float* kg,
+                       const float* qg, const float* gc_last, const float* h0, float* o,
+                       float* h_final, float* h_pre_all, float* v_new_all, int B, int H, int nc,
+                       int BT, int D, float scale, float clip, void* stream);
+int gdn2_stage_dhu(const float* dout, const float* dv_partial, const float* w_pseudo,
+                   const float* qg, const float* kg, const float* gc_last, const float* dht,
+                   float* dh_all, float* dh0, float* dv_all, int B, int H, int nc, int BT, int D,
+                   float scale, float clip, void* stream);
+int gdn2_stage_dav(const float* aqk, const float* v_new, const float* dout, float* daqk,
+                   float* dv, int n_chunks, int BT, int D, float clip, void* stream);
+int gdn2_stage_wy_dqkg(const float* q, const float* k, const float* b, const float* w,
+                       const float* v, const float* gc, const float* a, const float* h_pre,
+                       const float* v_new, const float* dout, const float* dv,
+                       const float* dh_next, float* dq, float* dk, float* db, float* dw,
+                       float* dv_raw, float* dgc, float* dakk, float* scratch, int n_chunks,
+                       int BT, int D, float scale, float clip, void* stream);
+int gdn2_stage_intra_bwd(int dtype, const float* daqkT, const float* dakkT, const void* q,
+                         const void* k, const void* b, const void* g, const float* zeros,
+                         float* dq, float* dk, float* db, float* dgc, int B, int T, int H, int D,
+                         int BT, int BC, float scale, float clip, void* stream);
+int gdn2_stage_revcumsum(const float* dgc, float* dg, int n_chunks, int BT, int D, float clip,
+                         void* stream);
+
 /* Token-by-token decode of a short segment (B, T, H, D), carrying the state
  * h0 (B,H,D,D, may be NULL = zero) to h_final: the recurrence of
  * gdn2_pallas_forward (gdn2_fwd.py:338-362, state API gdn2_fwd.py:400-404)

@@ -104,6 +104,36 @@ def test_copy_heads_rejects_bad_ranges_without_gpu_work():
     assert lib.gdn2_copy_heads(h, d, 0, 6, 0, 2, 512, 0, None) == _lib.OK            # nothing to move
 
 
+def test_stage_entry_points_reject_bad_arguments_without_gpu_work():
+    lib = _lib.load()
+    p = ctypes.c_void_p(4096)
+    assert lib.gdn2_stage_scores(0, None, p, p, p, p, p, 1, 128, 1, 128, 64, 0.1, 1e4, None) \
+        == _lib.ERR_INVALID
+    assert lib.gdn2_stage_scores(0, p, p, p, p, p, p, 1, 128, 1, 128, 256, 0.1, 1e4, None) \
+        == _lib.ERR_INVALID                                   # BT 64 or 128
+    assert lib.gdn2_stage_wy_solve(p, p, 4, 64, 8, 1e4, None) == _lib.ERR_INVALID   # BC % 16
+    assert lib.gdn2_stage_revcumsum(None, p, 4, 64, 128, 1e4, None) == _lib.ERR_INVALID
+    assert lib.gdn2_stage_dav(p, p, p, p, p, 0, 64, 128, 1e4, None) == _lib.ERR_INVALID
+    assert b"gdn2_stage" in lib.gdn2_last_error()
+
+
+def test_stage_functions_have_the_reference_names():
+    """gdn2_pipeline.py:14-31 imports these from gdn2_fwd / gdn2_bwd."""
+    from gdn2_package import gdn2_bwd, gdn2_fwd
+    for n in ("build_chunk_scores_pallas", "wy_solve_pallas", "recompute_wy_pallas",
+              "gdn2_inter_chunk_combine", "gdn2_inter_chunk_combine_with_state"):
+        assert callable(getattr(gdn2_fwd, n)), n
+    for n in ("reverse_cumsum_bwd", "gdn2_dhu_backward", "dav_backward_pallas",
+              "wy_dqkg_backward_pallas", "intra_backward_pallas"):
+        assert callable(getattr(gdn2_bwd, n)), n
+    gdn2_fwd.BT = 256
+    try:
+        with pytest.raises(gdn2_fwd.Gdn2ShapeError):
+            gdn2_fwd._stage_bt()
+    finally:
+        gdn2_fwd.BT = 256
+
+
 def test_streamed_head_group_fills_the_gpu():
     from gdn2_package.streaming import _head_group
     assert _head_group(1, 8192, 6) == 3      # 64 chunks x 3 heads >= 148 CTAs
