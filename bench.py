@@ -123,7 +123,7 @@ def step_work(cfg):
 # capture at B=1 (384 chunks, inputs larger than L2); traffic grows with the
 # chunk count, so a full launch moves this figure x 3072 chunks.
 NCU_TRAFFIC_PER_CHUNK = {"fwd_intra": 738_587, "bwd_intra1": 960_509, "bwd_intra2": 1_199_761,
-                         "bwd_intra3": 944_667}
+                         "bwd_intra3": 953_457}
 
 
 class ClockSampler:
