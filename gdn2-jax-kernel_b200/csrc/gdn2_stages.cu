@@ -42,16 +42,18 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
 k_stage_scores(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ b,
                const T* __restrict__ g, float* __restrict__ aqk, float* __restrict__ akk, int Tn,
-               int H, int D, int BT, float scale, float clip) {
+               int H, int D, int BT, float scale, float clip, bool k_resident) {
   extern __shared__ __align__(16) float sm[];
   float* gc = sm;
-  float* ks = sm + BT * D;
+  float* ks = k_resident ? sm + BT * D : nullptr;   // k of the chunk, when it fits
   const int nc = Tn / BT;
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % nc), h = (int)((chunk / nc) % H), bb = (int)(chunk / nc / H);
   const long rs = (long)H * D;
   const long off = ((long)bb * Tn + (long)c * BT) * rs + (long)h * D;
-  for (int e = threadIdx.x; e < BT * D; e += kThreads) ks[e] = to_f<T>(k[off + (e / D) * rs + e % D]);
+  auto kat = [&](int r, int d) { return ks ? ks[r * D + d] : to_f<T>(k[off + r * rs + d]); };
+  if (ks)
+    for (int e = threadIdx.x; e < BT * D; e += kThreads) ks[e] = to_f<T>(k[off + (e / D) * rs + e % D]);
   chunk_cumsum(g + off, rs, BT, D, gc);
   float* ao = aqk + chunk * BT * BT;
   float* ko = akk + chunk * BT * BT;
@@ -61,9 +63,9 @@ k_stage_scores(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     if (j <= i) {
       for (int d = 0; d < D; ++d) {
         const float ed = expf(fminf(fmaxf(gc[i * D + d] - gc[j * D + d], -kPairClip), kPairClip));
-        const float kj = ks[j * D + d] * ed;
+        const float kj = kat(j, d) * ed;
         sq = fmaf(to_f<T>(q[off + i * rs + d]), kj, sq);
-        sk = fmaf(to_f<T>(b[off + i * rs + d]) * ks[i * D + d], kj, sk);
+        sk = fmaf(to_f<T>(b[off + i * rs + d]) * kat(i, d), kj, sk);
       }
     }
     ao[e] = j <= i ? san(scale * sq, clip) : 0.f;
@@ -92,6 +94,64 @@ k_stage_wy(const float* __restrict__ akk, float* __restrict__ a, int bc, float c
   for (int e = threadIdx.x; e < C * C; e += kThreads) dst[e] = S[(e % C) * LD + e / C];
 }
 
+// Chunks too large for one shared tile (BT = 256): the BC diagonal blocks are
+// solved as above (one CTA per block; the reference's _block_solve), then
+// k_stage_wy_compose runs the substitution across the BC sub-blocks in the
+// reference's order (its Kernel B for two sub-blocks, gdn2_fwd.py:228-243,
+// continued for more), in global memory with one BC x BC scratch per chunk:
+//   A_mn = san(-A_mm acc),  acc = san(acc + T_mk A_kn) for k = n .. m-1.
+template <int C>
+__global__ void __launch_bounds__(kThreads)
+k_stage_wy_diag(const float* __restrict__ akk, float* __restrict__ a, int BT, float clip) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int LD = C + 4;
+  float* S = sm;
+  float* tmp = sm + C * LD;
+  const int nsub = BT / C;
+  const size_t chunk = blockIdx.x / nsub;
+  const int m = blockIdx.x % nsub;
+  const float* src = akk + chunk * BT * BT + (size_t)m * C * BT + m * C;
+  for (int e = threadIdx.x; e < C * C; e += kThreads) S[(e % C) * LD + e / C] = src[(e / C) * BT + e % C];
+  __syncthreads();
+  wy_inverse_T<C>(S, LD, tmp, C, clip);
+  __syncthreads();
+  float* dst = a + chunk * BT * BT + (size_t)m * C * BT + m * C;
+  for (int e = threadIdx.x; e < C * C; e += kThreads) dst[(e / C) * BT + e % C] = S[(e % C) * LD + e / C];
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_stage_wy_compose(const float* __restrict__ akk, float* __restrict__ a, float* __restrict__ scr,
+                   int BT, int BC, float clip) {
+  const size_t chunk = blockIdx.x;
+  const float* T = akk + chunk * BT * BT;
+  float* A = a + chunk * BT * BT;
+  float* acc = scr + chunk * BC * BC;
+  const int nsub = BT / BC;
+  for (int m = 1; m < nsub; ++m) {
+    for (int n = m - 1; n >= 0; --n) {
+      for (int e = threadIdx.x; e < BC * BC; e += kThreads) acc[e] = 0.f;
+      __syncthreads();
+      for (int kk = n; kk < m; ++kk) {
+        for (int e = threadIdx.x; e < BC * BC; e += kThreads) {
+          const int i = e / BC, j = e % BC;
+          float s = 0.f;
+          for (int x = 0; x < BC; ++x)
+            s = fmaf(T[(size_t)(m * BC + i) * BT + kk * BC + x], A[(size_t)(kk * BC + x) * BT + n * BC + j], s);
+          acc[e] = san(acc[e] + s, clip);
+        }
+        __syncthreads();
+      }
+      for (int e = threadIdx.x; e < BC * BC; e += kThreads) {
+        const int i = e / BC, j = e % BC;
+        float s = 0.f;
+        for (int x = 0; x < BC; ++x) s = fmaf(A[(size_t)(m * BC + i) * BT + m * BC + x], acc[x * BC + j], s);
+        A[(size_t)(m * BC + i) * BT + n * BC + j] = san(-s, clip);
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel C (gdn2_fwd.py:264-295): W = san(A (b k e^gc)), U = san(A (w v)),
 // kg = san(k e^{gc_last - gc}), qg = san(q e^gc), gc_last = san(gc_last).
@@ -102,10 +162,10 @@ k_stage_recompute(const T* __restrict__ q, const T* __restrict__ k, const T* __r
                   const T* __restrict__ w, const T* __restrict__ b, const T* __restrict__ g,
                   const float* __restrict__ a, float* __restrict__ wp, float* __restrict__ u,
                   float* __restrict__ kg, float* __restrict__ qg, float* __restrict__ gcl, int Tn,
-                  int H, int D, int BT, float clip) {
+                  int H, int D, int BT, float clip, bool wv_resident) {
   extern __shared__ __align__(16) float sm[];
-  float* gc = sm;            // then b k e^gc
-  float* wv = sm + BT * D;
+  float* gc = sm;                                      // then b k e^gc
+  float* wv = wv_resident ? sm + BT * D : nullptr;     // w v, when it fits
   const int nc = Tn / BT;
   const size_t chunk = blockIdx.x;
   const int c = (int)(chunk % nc), h = (int)((chunk / nc) % H), bb = (int)(chunk / nc / H);
@@ -119,7 +179,7 @@ k_stage_recompute(const T* __restrict__ q, const T* __restrict__ k, const T* __r
     const long x = off + i * rs + d;
     kg[co + e] = san(to_f<T>(k[x]) * expf(gl - gi), clip);
     qg[co + e] = san(to_f<T>(q[x]) * expf(gi), clip);
-    wv[e] = to_f<T>(w[x]) * to_f<T>(v[x]);
+    if (wv) wv[e] = to_f<T>(w[x]) * to_f<T>(v[x]);
   }
   for (int d = threadIdx.x; d < D; d += kThreads) gcl[chunk * D + d] = san(gc[(BT - 1) * D + d], clip);
   __syncthreads();
@@ -135,7 +195,8 @@ k_stage_recompute(const T* __restrict__ q, const T* __restrict__ k, const T* __r
     for (int j = 0; j < BT; ++j) {
       const float aij = ac[i * BT + j];
       sw = fmaf(aij, gc[j * D + d], sw);
-      su = fmaf(aij, wv[j * D + d], su);
+      su = fmaf(aij, wv ? wv[j * D + d] : to_f<T>(w[off + j * rs + d]) * to_f<T>(v[off + j * rs + d]),
+                su);
     }
     wp[co + e] = san(sw, clip);
     u[co + e] = san(su, clip);
@@ -429,7 +490,10 @@ k_stage_revcumsum(const float* __restrict__ dgc, float* __restrict__ dg, int BT,
 namespace {
 using namespace gdn2;
 
-bool shape_ok(int BT, int D) { return (BT == 64 || BT == 128) && (D == 64 || D == 128); }
+bool shape_ok(int BT, int D) {
+  return (BT == 64 || BT == 128 || BT == 256) && (D == 64 || D == 128);
+}
+constexpr size_t kSmemMax = 200 * 1024;   // resident-tile budget of the stage kernels
 
 int bad(const char* what) { return report_error(GDN2_ERR_INVALID, what); }
 
@@ -461,30 +525,49 @@ int gdn2_stage_scores(int dtype, const void* q, const void* k, const void* b, co
                       float clip, void* stream) {
   if (!dims_ok(B, T, H, D, BT) || !q || !k || !b || !g || !aqk || !akk)
     return bad("gdn2_stage_scores: bad shape or null pointer");
-  const size_t smem = 2 * (size_t)BT * D * sizeof(float);
+  const bool kres = 2 * (size_t)BT * D * sizeof(float) <= kSmemMax;
+  const size_t smem = (kres ? 2 : 1) * (size_t)BT * D * sizeof(float);
   const unsigned n = (unsigned)B * H * (T / BT);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == GDN2_F32) {
     if (int rc = smem_attr(k_stage_scores<float>, smem)) return rc;
     k_stage_scores<float><<<n, kThreads, smem, s>>>(
         (const float*)q, (const float*)k, (const float*)b, (const float*)g, aqk, akk, T, H, D, BT,
-        scale, clip);
+        scale, clip, kres);
   } else if (dtype == GDN2_BF16) {
     using bf = __nv_bfloat16;
     if (int rc = smem_attr(k_stage_scores<bf>, smem)) return rc;
     k_stage_scores<bf><<<n, kThreads, smem, s>>>((const bf*)q, (const bf*)k, (const bf*)b,
-                                                 (const bf*)g, aqk, akk, T, H, D, BT, scale, clip);
+                                                 (const bf*)g, aqk, akk, T, H, D, BT, scale, clip,
+                                                 kres);
   } else {
     return bad("gdn2_stage_scores: dtype");
   }
   return launched("gdn2_stage_scores");
 }
 
-int gdn2_stage_wy_solve(const float* akk, float* a, int n_chunks, int BT, int BC, float clip,
-                        void* stream) {
-  if (!akk || !a || n_chunks <= 0 || (BT != 64 && BT != 128) || BC <= 0 || BC % 16 || BT % BC)
+int gdn2_stage_wy_solve(const float* akk, float* a, float* scratch, int n_chunks, int BT, int BC,
+                        float clip, void* stream) {
+  if (!akk || !a || n_chunks <= 0 || (BT != 64 && BT != 128 && BT != 256) || BC <= 0 || BC % 16 ||
+      BT % BC || (BT == 256 && (BC > 128 || !scratch)))
     return bad("gdn2_stage_wy_solve: bad shape or null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (BT == 256) {   // diagonal blocks in shared memory, then the cross-block substitution
+    if (cudaMemsetAsync(a, 0, (size_t)n_chunks * BT * BT * sizeof(float), s) != cudaSuccess)
+      return launched("gdn2_stage_wy_solve");
+    const unsigned nb = (unsigned)n_chunks * (BT / BC);
+    const size_t smem = ((size_t)BC * (BC + 4) + (size_t)BC * BC / 4) * sizeof(float);
+#define GDN2_DIAG(CC)                                                                   \
+    if (BC == CC) {                                                                     \
+      if (int rc = smem_attr(k_stage_wy_diag<CC>, smem)) return rc;                     \
+      k_stage_wy_diag<CC><<<nb, kThreads, smem, s>>>(akk, a, BT, clip);                 \
+    }
+    GDN2_DIAG(16) GDN2_DIAG(32) GDN2_DIAG(64) GDN2_DIAG(128)
+#undef GDN2_DIAG
+    if (int rc = launched("gdn2_stage_wy_solve")) return rc;
+    k_stage_wy_compose<<<n_chunks, kThreads, 0, s>>>(akk, a, scratch, BT, BC, clip);
+    return launched("gdn2_stage_wy_solve");
+  }
   const size_t smem = ((size_t)BT * (BT + 4) + (size_t)BT * BT / 4) * sizeof(float);
   if (BT == 64) {
     if (int rc = smem_attr(k_stage_wy<64>, smem)) return rc;
@@ -503,21 +586,22 @@ int gdn2_stage_recompute_wy(int dtype, const void* q, const void* k, const void*
   if (!dims_ok(B, T, H, D, BT) || !q || !k || !v || !w || !b || !g || !a || !w_pseudo || !u ||
       !kg || !qg || !gc_last)
     return bad("gdn2_stage_recompute_wy: bad shape or null pointer");
-  const size_t smem = 2 * (size_t)BT * D * sizeof(float);
+  const bool wres = 2 * (size_t)BT * D * sizeof(float) <= kSmemMax;
+  const size_t smem = (wres ? 2 : 1) * (size_t)BT * D * sizeof(float);
   const unsigned n = (unsigned)B * H * (T / BT);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == GDN2_F32) {
     if (int rc = smem_attr(k_stage_recompute<float>, smem)) return rc;
     k_stage_recompute<float><<<n, kThreads, smem, s>>>(
         (const float*)q, (const float*)k, (const float*)v, (const float*)w, (const float*)b,
-        (const float*)g, a, w_pseudo, u, kg, qg, gc_last, T, H, D, BT, clip);
+        (const float*)g, a, w_pseudo, u, kg, qg, gc_last, T, H, D, BT, clip, wres);
   } else if (dtype == GDN2_BF16) {
     using bf = __nv_bfloat16;
     if (int rc = smem_attr(k_stage_recompute<bf>, smem)) return rc;
     k_stage_recompute<bf><<<n, kThreads, smem, s>>>((const bf*)q, (const bf*)k, (const bf*)v,
                                                     (const bf*)w, (const bf*)b, (const bf*)g, a,
                                                     w_pseudo, u, kg, qg, gc_last, T, H, D, BT,
-                                                    clip);
+                                                    clip, wres);
   } else {
     return bad("gdn2_stage_recompute_wy: dtype");
   }

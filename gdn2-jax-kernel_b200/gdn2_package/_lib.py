@@ -46,7 +46,7 @@ SIGNATURES = {
     "gdn2_diag_enable": (_i, [_i]),
     "gdn2_pair64_enable": (_i, [_i]),
     "gdn2_stage_scores": (_i, [_i] + [_vp] * 6 + [_i] * 5 + [_f, _f, _vp]),
-    "gdn2_stage_wy_solve": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),
+    "gdn2_stage_wy_solve": (_i, [_vp, _vp, _vp, _i, _i, _i, _f, _vp]),
     "gdn2_stage_recompute_wy": (_i, [_i] + [_vp] * 12 + [_i] * 5 + [_f, _vp]),
     "gdn2_stage_combine": (_i, [_vp] * 11 + [_i] * 5 + [_f, _f, _vp]),
     "gdn2_stage_dhu": (_i, [_vp] * 10 + [_i] * 5 + [_f, _f, _vp]),

@@ -280,12 +280,12 @@ def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_t
 # Separate entry points on the reference's chunked layouts, for code that
 # composes the stages itself (gdn2_pipeline.py:14-31 imports them).  Each runs
 # one CUDA kernel of libgdn2.so (gdn2_stage_*); the fused forward above does
-# not use them.  BT, BC, CLIP are read at call time; BT is 64 or 128.
+# not use them.  BT, BC, CLIP are read at call time; BT is 64, 128 or 256.
 
 def _stage_bt():
     bt = int(BT)
-    if bt not in (64, 128):
-        raise Gdn2ShapeError(f"the stage functions run BT = 64 or 128; got BT={bt}")
+    if bt not in (64, 128, 256):
+        raise Gdn2ShapeError(f"the stage functions run BT = 64, 128 or 256; got BT={bt}")
     return bt
 
 
@@ -343,7 +343,10 @@ def wy_solve_pallas(Akk):
     akk = _f32(Akk, dev)
     a = torch.empty_like(akk)
     n = akk.numel() // (bt * bt)
-    rc = _lib.load().gdn2_stage_wy_solve(akk.data_ptr(), a.data_ptr(), n, bt, int(BC),
+    bc = int(BC)
+    scr = torch.empty((n, bc, bc), dtype=torch.float32, device=dev) if bt == 256 else None
+    rc = _lib.load().gdn2_stage_wy_solve(akk.data_ptr(), a.data_ptr(),
+                                         scr.data_ptr() if scr is not None else None, n, bt, bc,
                                          float(CLIP), _stream(dev))
     _lib.check(rc, "wy_solve_pallas")
     return a
@@ -373,7 +376,7 @@ def _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, with_state, debug_tag
     wp = torch.as_tensor(w_pseudo)
     dev = wp.device if wp.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
     B, H, nc, bt, D = wp.shape
-    if D not in _SUPPORTED_D or bt not in (64, 128):
+    if D not in _SUPPORTED_D or bt not in (64, 128, 256):
         raise Gdn2ShapeError(f"unsupported chunk tiles {tuple(wp.shape)}")
     xs = [_f32(t, dev) for t in (Aqk, w_pseudo, u, kg, qg, gc_last)]
     h0 = None if h0 is None else _f32(h0, dev)

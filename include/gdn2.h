@@ -174,10 +174,12 @@ int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, siz
 
 /* The reference's stage functions as separate entry points, on its chunked
  * layouts: (B, H, nc, BT, .) float32 tiles, gc_last (B, H, nc, D), inputs
- * q..g (B, T, H, D) of `dtype` where named.  The fused gdn2_fwd / gdn2_bwd
+ * q..g (B, T, H, D) of `dtype` where named; BT 64, 128 or 256.  The fused gdn2_fwd / gdn2_bwd
  * never call them.  Each replaces the reference function of the same name:
  *   gdn2_stage_scores        build_chunk_scores_pallas (gdn2_fwd.py:142-170)
- *   gdn2_stage_wy_solve      wy_solve_pallas (gdn2_fwd.py:246-260), any BT/BC
+ *   gdn2_stage_wy_solve      wy_solve_pallas (gdn2_fwd.py:246-260), any BC;
+ *                            BT = 256 needs BC <= 128 and n_chunks*BC*BC
+ *                            floats of scratch (NULL otherwise)
  *   gdn2_stage_recompute_wy  recompute_wy_pallas (gdn2_fwd.py:298-330)
  *   gdn2_stage_combine       gdn2_inter_chunk_combine(_with_state)
  *                            (gdn2_fwd.py:338-397); h_pre_all (nc,B,H,D,D) and
@@ -193,8 +195,8 @@ int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, siz
 int gdn2_stage_scores(int dtype, const void* q, const void* k, const void* b, const void* g,
                       float* aqk, float* akk, int B, int T, int H, int D, int BT, float scale,
                       float clip, void* stream);
-int gdn2_stage_wy_solve(const float* akk, float* a, int n_chunks, int BT, int BC, float clip,
-                        void* stream);
+int gdn2_stage_wy_solve(const float* akk, float* a, float* scratch, int n_chunks, int BT, int BC,
+                        float clip, void* stream);
 int gdn2_stage_recompute_wy(int dtype, const void* q, const void* k, const void* v, const void* w,
                             const void* b, const void* g, const float* a, float* w_pseudo,
                             float* u, float* kg, float* qg, float* gc_last, int B, int T, int H,

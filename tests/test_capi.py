@@ -109,9 +109,10 @@ def test_stage_entry_points_reject_bad_arguments_without_gpu_work():
     p = ctypes.c_void_p(4096)
     assert lib.gdn2_stage_scores(0, None, p, p, p, p, p, 1, 128, 1, 128, 64, 0.1, 1e4, None) \
         == _lib.ERR_INVALID
-    assert lib.gdn2_stage_scores(0, p, p, p, p, p, p, 1, 128, 1, 128, 256, 0.1, 1e4, None) \
-        == _lib.ERR_INVALID                                   # BT 64 or 128
-    assert lib.gdn2_stage_wy_solve(p, p, 4, 64, 8, 1e4, None) == _lib.ERR_INVALID   # BC % 16
+    assert lib.gdn2_stage_scores(0, p, p, p, p, p, p, 1, 128, 1, 128, 512, 0.1, 1e4, None) \
+        == _lib.ERR_INVALID                                   # BT 64, 128 or 256
+    assert lib.gdn2_stage_wy_solve(p, p, p, 4, 64, 8, 1e4, None) == _lib.ERR_INVALID   # BC % 16
+    assert lib.gdn2_stage_wy_solve(p, p, None, 4, 256, 128, 1e4, None) == _lib.ERR_INVALID  # scratch
     assert lib.gdn2_stage_revcumsum(None, p, 4, 64, 128, 1e4, None) == _lib.ERR_INVALID
     assert lib.gdn2_stage_dav(p, p, p, p, p, 0, 64, 128, 1e4, None) == _lib.ERR_INVALID
     assert b"gdn2_stage" in lib.gdn2_last_error()
@@ -126,7 +127,7 @@ def test_stage_functions_have_the_reference_names():
     for n in ("reverse_cumsum_bwd", "gdn2_dhu_backward", "dav_backward_pallas",
               "wy_dqkg_backward_pallas", "intra_backward_pallas"):
         assert callable(getattr(gdn2_bwd, n)), n
-    gdn2_fwd.BT = 256
+    gdn2_fwd.BT = 512
     try:
         with pytest.raises(gdn2_fwd.Gdn2ShapeError):
             gdn2_fwd._stage_bt()

@@ -16,7 +16,8 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
 
 NAMES = ("q", "k", "v", "w", "b", "g")
-CASES = [(64, 16, 1e4), (128, 64, 1e4), (64, 32, 0.5)]   # BT, BC, CLIP (0.5: clips act)
+CASES = [(64, 16, 1e4), (128, 64, 1e4), (64, 32, 0.5),   # BT, BC, CLIP (0.5: clips act)
+         (256, 128, 1e4), (256, 64, 0.5)]                  # BT = 256: the reference's default
 
 
 def rel(a, b):
@@ -105,7 +106,7 @@ def test_backward_stages_vs_oracle(BT, BC, clip):
     assert rel(dg, O.reverse_cumsum(dgc_tot, clip)) < 1e-4
 
 
-@pytest.mark.parametrize("BT,BC", [(64, 16), (128, 64)])
+@pytest.mark.parametrize("BT,BC", [(64, 16), (128, 64), (256, 128)])
 def test_reference_pipeline_from_stages(BT, BC):
     """_gdn2_core_bwd (gdn2_pipeline.py:70-137) written with the stage
     functions gives the fused backward's gradients."""
