@@ -6,7 +6,6 @@
 // library instead of from the caller.
 #include <stdio.h>
 
-#include <mutex>
 
 #include "../../include/gdn2.h"
 
@@ -23,31 +22,19 @@ constexpr size_t kScratchBytes = GDN2_NOALLOC_SCRATCH_BYTES;
 // its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_addr[kMaxDevices] = {};
-
-// Device address of the scratch on the current device, looked up once per
-// device with that device current.
+// Device address of the scratch on the current device.  Looked up on every
+// call (cheap), so the address stays valid across a cudaDeviceReset or a new
+// context on the device.
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return gdn2::report_error(GDN2_ERR_CUDA, cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices)
-    return gdn2::report_error(GDN2_ERR_INVALID, "gdn2_fwd_noalloc: device index out of range");
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      char msg[256];
-      snprintf(msg, sizeof(msg), "gdn2_fwd_noalloc: cudaGetSymbolAddress failed: %s",
-               cudaGetErrorString(e));
-      return gdn2::report_error(GDN2_ERR_CUDA, msg);
-    }
-    g_addr[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "gdn2_fwd_noalloc: cudaGetSymbolAddress failed: %s",
+             cudaGetErrorString(e));
+    return gdn2::report_error(GDN2_ERR_CUDA, msg);
   }
-  *out = g_addr[dev];
+  *out = p;
   return GDN2_OK;
 }
 
