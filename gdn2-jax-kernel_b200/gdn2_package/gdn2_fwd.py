@@ -25,7 +25,7 @@ from . import _lib
 
 # ---------- constants (gdn2_fwd.py:29-33) ----------
 BT = 256     # chunk length
-BC = 128     # sub-block length (the reference's clip granularity; results do not depend on it)
+BC = 128     # sub-block length: where the WY solve and B4 sanitise (results depend on it only where a clip acts)
 MB = 16      # micro-block of the triangular solve
 CLIP = 1e4   # stage sanitiser bound
 # Chunk length policy.  EXACT_BT = True (default) runs chunks of BT itself
