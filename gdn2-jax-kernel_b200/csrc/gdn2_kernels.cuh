@@ -333,6 +333,10 @@ __device__ __forceinline__ void wy_inverse_T128(float* S, int ld, float* tmp, fl
     }
   }
   __syncthreads();
+#ifdef GDN2_PHASE_TIMING
+  if (blockIdx.x == gridDim.x / 2 && threadIdx.x == 0)
+    printf("wy phases: micro %lld in-block %lld last %lld\n", wy_t[0], wy_t[1], clock64() - t2);
+#endif
 }
 
 // Reverse (suffix) column sum of a C x D tile in shared memory (ld = D),
