@@ -490,8 +490,11 @@ k_stage_revcumsum(const float* __restrict__ dgc, float* __restrict__ dg, int BT,
 namespace {
 using namespace gdn2;
 
+// D = 256 (beyond the reference's D = 128, gdn2_fwd.py:145) with BT <= 128:
+// the per-chunk gc tile of 256 x 256 floats would not fit shared memory.
 bool shape_ok(int BT, int D) {
-  return (BT == 64 || BT == 128 || BT == 256) && (D == 64 || D == 128);
+  return (BT == 64 || BT == 128 || BT == 256) && (D == 64 || D == 128 || D == 256) &&
+         !(D == 256 && BT == 256);
 }
 constexpr size_t kSmemMax = 200 * 1024;   // resident-tile budget of the stage kernels
 

@@ -13,6 +13,8 @@ import torch
 from . import _lib
 from . import gdn2_fwd as _fwd
 
+_FINAL_CLIP = 1e4  # gdn2_pipeline.py:34
+
 
 def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
     """Cotangents (dq, dk, dv, dw, db, dg, dh0) of (o, h_final) w.r.t. the
@@ -23,6 +25,8 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
     (``gdn2_pallas_forward_trainable`` does this) to skip the recompute of
     the forward; without it the forward is recomputed as in the reference.
     """
+    if _fwd._head_dim(q) in _fwd._STAGE_D:
+        return _stage_backward(q, k, v, w, b, g, scale, h0, dout, dh_final)
     p = _fwd._Prepared(q, k, v, w, b, g, scale, h0)
     dev = p.dev
     do = torch.as_tensor(dout).to(device=dev, dtype=torch.float32, non_blocking=True).contiguous()
@@ -155,3 +159,48 @@ def intra_backward_pallas(dAqk, dAkk, q, k, b, g, scale):
                                           _fwd._stream(dev))
     _lib.check(rc, "intra_backward_pallas")
     return tuple(outs)
+
+
+def _stage_backward(q, k, v, w, b, g, scale, h0, dout, dh_final):
+    """Backward of a head dim the fused kernels do not cover (D = 256): the
+    reference's _gdn2_core_bwd (gdn2_pipeline.py:70-137) composed of the
+    stage kernels, with the final +-1e4 sanitiser and the input dtypes."""
+    q_t = torch.as_tensor(q)
+    B, L, H, D, bt = _fwd._check_seq(q_t)
+    nc = L // bt
+    (qd, kd, vd, wd, bd, gd), _, dev = _fwd._stage_in((q, k, v, w, b, g))
+    f32 = lambda t: None if t is None else _fwd._f32(t, dev)
+    h0d, do, dhf = f32(h0), f32(dout), f32(dh_final)
+    if tuple(do.shape) != (B, L, H, D):
+        raise _fwd.Gdn2ShapeError(f"dout must be {(B, L, H, D)}")
+    if dhf is None:
+        dhf = torch.zeros((B, H, D, D), dtype=torch.float32, device=dev)
+    Aqk, Akk = _fwd.build_chunk_scores_pallas(qd, kd, bd, gd, scale)
+    A = _fwd.wy_solve_pallas(Akk)
+    wp, u, kg, qg, gcl = _fwd.recompute_wy_pallas(qd, kd, vd, wd, bd, gd, A)
+    _, _, hpre, vall = _fwd.gdn2_inter_chunk_combine_with_state(Aqk, wp, u, kg, qg, gcl, scale, h0d)
+    hpre, vall = hpre.permute(1, 2, 0, 3, 4), vall.permute(1, 2, 0, 3, 4)
+    ch = lambda t: t.float().reshape(B, nc, bt, H, D).permute(0, 3, 1, 2, 4).contiguous()
+    # gc = in-chunk cumsum of g (gdn2_pipeline.py:94-96)
+    gc = torch.cumsum(ch(gd).double(), dim=-2).float()
+    dAqk, dvp = dav_backward_pallas(Aqk, vall, ch(do))
+    dh_all, dh0, dv_all = gdn2_dhu_backward(ch(do), dvp, wp, qg, kg, gcl, scale, dht=dhf)
+    dh_next = torch.cat([dh_all[:, :, 1:], dhf[:, :, None]], dim=2)   # gdn2_pipeline.py:52-56
+    b3 = wy_dqkg_backward_pallas(ch(qd), ch(kd), ch(bd), ch(wd), ch(vd), gc, A, Akk, hpre, vall,
+                                 ch(do), dv_all, dh_next, scale)
+    dq4, dk4, db4, dgc4 = intra_backward_pallas(dAqk, b3["dAkk"], qd, kd, bd, gd, scale)
+    dg = reverse_cumsum_bwd(b3["dgc"] + dgc4, bt)
+    unch = lambda t: t.permute(0, 2, 3, 1, 4).reshape(B, L, H, D)
+    fin = lambda t: torch.nan_to_num(t.clamp(-_FINAL_CLIP, _FINAL_CLIP), nan=0.0,
+                                     posinf=_FINAL_CLIP, neginf=-_FINAL_CLIP)
+    grads = [fin(unch(t)) for t in (b3["dq"] + dq4, b3["dk"] + dk4, b3["dv_raw"], b3["dw"],
+                                    b3["db"] + db4, dg)]
+    ins = [torch.as_tensor(t) for t in (q, k, v, w, b, g)]
+    grads = [t.to(x.dtype) for t, x in zip(grads, ins)]
+    dh0 = fin(dh0)
+    if h0 is not None:
+        dh0 = dh0.to(torch.as_tensor(h0).dtype)
+    if ins[0].device.type != "cuda":
+        grads = [t.cpu() for t in grads]
+        dh0 = dh0.cpu()
+    return (*grads, dh0)

@@ -59,7 +59,8 @@ GATES = "activated"
 
 _GDN2_FWD_DIAG = os.environ.get("GDN2_FWD_DIAG", "0") == "1"
 _KERNEL_CHUNKS = (128, 64)
-_SUPPORTED_D = (64, 128)
+_SUPPORTED_D = (64, 128)   # the fused kernels
+_STAGE_D = (256,)          # head dims served by the stage kernels alone (BT 64 or 128)
 
 
 class Gdn2ShapeError(ValueError, AssertionError):
@@ -230,6 +231,10 @@ def _run_forward(p, save_residuals=False, ws=None, debug_tag=""):
 def gdn2_pallas_forward(q, k, v, w, b, g, scale, h0=None, debug_tag=""):
     """Full forward: Kernels A -> B -> C -> D.  Returns o (B,T,H,D) float32
     and h_final (B,H,D,D) float32 (gdn2_fwd.py:400-424)."""
+    if _head_dim(q) in _STAGE_D:
+        o, h_final, _ = _stage_forward(q, k, v, w, b, g, scale, h0, debug_tag)
+        on_host = torch.as_tensor(q).device.type != "cuda"
+        return (o.cpu(), h_final.cpu()) if on_host else (o, h_final)
     p = _Prepared(q, k, v, w, b, g, scale, h0)
     o, h_final, _ = _run_forward(p, debug_tag=debug_tag)
     if p.on_host:
@@ -267,6 +272,11 @@ def gdn2_pallas_forward_with_residuals(q, k, v, w, b, g, scale, h0=None, debug_t
     Aqk, A, w_pseudo, u, kg, qg, gc_last, h_pre_all, v_new_all, all float32 in
     the batch-major (B, H, nc, ...) layout the backward consumes.  The
     reference additionally returns Akk, which the fused kernels never store."""
+    if _head_dim(q) in _STAGE_D:
+        o, h_final, res = _stage_forward(q, k, v, w, b, g, scale, h0, debug_tag, residuals=True)
+        if torch.as_tensor(q).device.type != "cuda":
+            return o.cpu(), h_final.cpu(), {n: t.cpu() for n, t in res.items()}
+        return o, h_final, res
     p = _Prepared(q, k, v, w, b, g, scale, h0)
     p.code |= _lib.NO_PAIR   # the residual views below follow the one-chunk tile layout
     o, h_final, ws = _run_forward(p, save_residuals=True, debug_tag=debug_tag)
@@ -309,9 +319,11 @@ def _stream(dev):
 
 def _check_seq(q):
     B, L, H, D = q.shape
-    if D not in _SUPPORTED_D:
-        raise Gdn2ShapeError(f"head dim D={D} unsupported (64 or 128)")
+    if D not in _SUPPORTED_D + _STAGE_D:
+        raise Gdn2ShapeError(f"head dim D={D} unsupported (64, 128 or 256)")
     bt = _stage_bt()
+    if D in _STAGE_D and bt == 256:
+        raise Gdn2ShapeError(f"D={D} runs BT = 64 or 128; got BT={bt}")
     if L % bt:
         raise Gdn2ShapeError(f"L={L} must be divisible by BT={bt}.")
     return B, L, H, D, bt
@@ -376,7 +388,7 @@ def _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, with_state, debug_tag
     wp = torch.as_tensor(w_pseudo)
     dev = wp.device if wp.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
     B, H, nc, bt, D = wp.shape
-    if D not in _SUPPORTED_D or bt not in (64, 128, 256):
+    if D not in _SUPPORTED_D + _STAGE_D or bt not in (64, 128, 256):
         raise Gdn2ShapeError(f"unsupported chunk tiles {tuple(wp.shape)}")
     xs = [_f32(t, dev) for t in (Aqk, w_pseudo, u, kg, qg, gc_last)]
     h0 = None if h0 is None else _f32(h0, dev)
@@ -405,3 +417,34 @@ def gdn2_inter_chunk_combine_with_state(Aqk, w_pseudo, u, kg, qg, gc_last, scale
     (nc, B, H, BT, D), chunk-major as the reference's scan stacks them
     (gdn2_fwd.py:369-397)."""
     return _combine(Aqk, w_pseudo, u, kg, qg, gc_last, scale, h0, True, debug_tag)
+
+
+# ---------- head dims beyond the fused kernels (D = 256) ----------
+
+def _head_dim(q):
+    shape = tuple(torch.as_tensor(q).shape)
+    return shape[-1] if len(shape) == 4 else None
+
+
+def _stage_forward(q, k, v, w, b, g, scale, h0=None, debug_tag="", residuals=False):
+    """Forward of a head dim the fused kernels do not cover (D = 256, beyond
+    the reference's D = 128, gdn2_fwd.py:145): the reference's own
+    composition of Kernels A-D (gdn2_fwd.py:400-457) on the stage kernels.
+    Returns o (B, T, H, D), h_final and, with ``residuals``, the
+    intermediates in the batch-major layout of the fused residuals."""
+    if GATES != "activated":
+        raise Gdn2ShapeError("raw gates need D = 64 or 128")
+    q = torch.as_tensor(q)
+    B, L, H, D, bt = _check_seq(q)
+    Aqk, Akk = build_chunk_scores_pallas(q, k, b, g, scale)
+    A = wy_solve_pallas(Akk)
+    wp, u, kg, qg, gcl = recompute_wy_pallas(q, k, v, w, b, g, A)
+    o, hf, hpre, vall = gdn2_inter_chunk_combine_with_state(Aqk, wp, u, kg, qg, gcl, scale, h0,
+                                                            debug_tag)
+    out = o.permute(0, 2, 3, 1, 4).reshape(B, L, H, D)
+    res = None
+    if residuals:
+        res = dict(Aqk=Aqk, A=A, w_pseudo=wp, u=u, kg=kg, qg=qg, gc_last=gcl,
+                   h_pre_all=hpre.permute(1, 2, 0, 3, 4), v_new_all=vall.permute(1, 2, 0, 3, 4),
+                   Akk=Akk)
+    return out, hf, res

@@ -23,6 +23,9 @@ _FINAL_CLIP = 1e4  # gdn2_pipeline.py:34
 
 def _gdn2_core_fwd(q, k, v, w, b, g, scale, h0, keep_residuals=True):
     """Forward rule: returns ((out, h_final), residuals) (gdn2_pipeline.py:64-67)."""
+    if _fwd._head_dim(q) in _fwd._STAGE_D:   # stage kernels; the backward recomputes
+        o, h_final = _fwd.gdn2_pallas_forward(q, k, v, w, b, g, scale, h0)
+        return (o, h_final), (q, k, v, w, b, g, h0, None)
     p = _fwd._Prepared(q, k, v, w, b, g, scale, h0)
     o, h_final, ws = _fwd._run_forward(p, save_residuals=keep_residuals)
     residuals = (q, k, v, w, b, g, h0, ws if keep_residuals else None)

@@ -138,3 +138,40 @@ def test_reference_pipeline_from_stages(BT, BC):
     fused = gdn2_backward(q, k, v, w, b, g, s, h0, do, dhf)
     for name, a, r in zip(("dq", "dk", "dv", "dw", "db", "dg", "dh0"), staged, fused):
         assert rel(a, r) < 1e-4, (name, rel(a, r))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("BT,BC,clip", [(64, 16, 1e4), (128, 64, 1e4), (64, 32, 0.5)])
+def test_head_dim_256_vs_oracle(BT, BC, clip, dtype):
+    """D = 256 (beyond the reference's D = 128) runs the reference's own
+    stage composition on the stage kernels: forward, all seven gradients and
+    the autograd path against the float64 oracle."""
+    from gdn2_package import gdn2_pallas_forward, gdn2_pallas_forward_trainable
+    gdn2_fwd.BT, gdn2_fwd.BC, gdn2_fwd.CLIP = BT, BC, clip
+    inp = make_inputs(1, 256, 2, 256, seed=12, h0_std=0.1)
+    args = [torch.as_tensor(inp[n]).to("cuda", dtype) for n in NAMES]
+    h0 = _cu(inp["h0"])
+    ref_in = [torch.as_tensor(inp[n]).to(dtype).double().numpy() for n in NAMES]
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    o, h = gdn2_pallas_forward(*args, inp["scale"], h0)
+    o_r, h_r = O.forward(*ref_in, inp["scale"], inp["h0"], BT, BC, clip)
+    assert rel(o, o_r) < tol and rel(h, h_r) < tol, (rel(o, o_r), rel(h, h_r))
+    grads = gdn2_backward(*args, inp["scale"], h0, _cu(inp["dout"]), _cu(inp["dh_final"]))
+    g_r = O.backward(*ref_in, inp["scale"], inp["h0"], inp["dout"], inp["dh_final"], BT, BC, clip)
+    for name, a, r in zip(("dq", "dk", "dv", "dw", "db", "dg", "dh0"), grads, g_r):
+        assert rel(a, r) < tol, (name, rel(a, r))
+    xs = [a.clone().requires_grad_() for a in args]
+    h0g = h0.clone().requires_grad_()
+    o2, h2 = gdn2_pallas_forward_trainable(*xs, inp["scale"], h0g)
+    torch.autograd.backward((o2, h2), (_cu(inp["dout"]), _cu(inp["dh_final"])))
+    assert torch.equal(o2.detach(), o)
+    for a, b in zip([*(x.grad for x in xs), h0g.grad], grads):
+        assert torch.equal(a, b)
+
+
+def test_head_dim_256_shape_limits():
+    from gdn2_package import gdn2_pallas_forward
+    gdn2_fwd.BT, gdn2_fwd.BC = 256, 128
+    x = torch.zeros((1, 256, 1, 256), device="cuda")
+    with pytest.raises(gdn2_fwd.Gdn2ShapeError):
+        gdn2_pallas_forward(x, x, x, x, x, x, 0.06)
