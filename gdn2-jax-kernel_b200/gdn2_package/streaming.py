@@ -76,12 +76,15 @@ def _head_group(Bs, T, H, D=128):
 
 
 def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, shard=1, depth=3,
-                 out=None, heads=None):
+                 out=None, heads=None, edges=True):
     """Forward and backward of one layer call (forward only when ``dout`` is
     None; a missing ``dh_final`` is zero).  Host tensors (pinned for
     asynchronous copies) are streamed in shards of ``shard`` batch rows by
     ``heads`` heads (default: the smallest group that fills the GPU), each
-    tensor moved by one pitched copy, with ``depth`` shards in flight; ``out`` may hold preallocated host outputs
+    tensor moved by one pitched copy, with ``depth`` shards in flight
+    (``edges``: the first and the last head group go as single heads, which
+    shortens the copy-in before the first kernels and the work after the
+    last copy-in); ``out`` may hold preallocated host outputs
     ``(o, h_final[, dq, dk, dv, dw, db, dg, dh0])``.  Gradients come back in
     the input dtype, o / h_final / dh0 in float32; the gradient tuple is None
     for a forward only."""
@@ -124,11 +127,16 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
         raise _fwd.Gdn2ShapeError(f"heads={Hs} must divide the head count H={H}")
     dev = torch.device("cuda", torch.cuda.current_device())
     # constants and chunking are validated exactly as for the device path
-    p = _fwd._Prepared(*[torch.zeros((Bs, T, Hs, D), dtype=dt, device=dev)] * 6, scale,
-                       None if h0_h is None else torch.empty((Bs, Hs, D, D), device=dev))
-    if p.C == 64 and D == 128 and T % 128 == 0 and _fwd.GATES == "activated" and \
-            bool((xs[5] > 0).any()):
-        p.code |= _lib.NO_PAIR   # as _Prepared decides for device tensors
+    no_pair = _fwd.GATES == "activated" and bool((xs[5] > 0).any())
+
+    def prepared(hs):
+        pp = _fwd._Prepared(*[torch.zeros((Bs, T, hs, D), dtype=dt, device=dev)] * 6, scale,
+                            None if h0_h is None else torch.empty((Bs, hs, D, D), device=dev))
+        if pp.C == 64 and D == 128 and T % 128 == 0 and no_pair:
+            pp.code |= _lib.NO_PAIR   # as _Prepared decides for device tensors
+        return pp
+
+    p = prepared(Hs)
     lib = _lib.load()
     if out is None:
         pin = torch.cuda.is_available()
@@ -141,7 +149,13 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
     o_h, hf_h, *g_h = out
     dh0_h = g_h.pop() if bwd else None
     nb, nhg = B // Bs, H // Hs
-    nsh = nb * nhg
+    plan = [(bi * Bs, gi * Hs, Hs) for bi in range(nb) for gi in range(nhg)]   # (b0, h0, heads)
+    if edges and Hs > 1 and len(plan) > 2:
+        first, last = plan[0], plan[-1]
+        plan = ([(first[0], first[1] + i, 1) for i in range(Hs)] + plan[1:-1]
+                + [(last[0], last[1] + i, 1) for i in range(Hs)])
+    preps = {hs: (p if hs == Hs else prepared(hs)) for hs in {x[2] for x in plan}}
+    nsh = len(plan)
     nslot = max(1, min(int(depth), nsh))
     slots = [_Slot(p, Bs, dev, h0_h is not None, bwd) for _ in range(nslot)]
     # each shard's status header (gdn2_workspace_status) lands in pinned memory
@@ -155,49 +169,51 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
     for st in (s_in, s_out, *s_runs):
         st.wait_stream(cur)
 
-    def copy(host, devt, b0, h0, seq, to_device, stream):
-        # one pitched DMA per tensor: rows (b, t) of the shard, heads h0 .. h0+Hs-1
+    def copy(host, devt, b0, h0, hs, seq, to_device, stream):
+        # one pitched DMA per tensor: rows (b, t) of the shard, heads h0 .. h0+hs-1
+        # (a shard of fewer heads than the slot uses the slot buffers' prefix)
         eb = host.element_size()
         head = (D if seq else D * D) * eb
         rows = Bs * (T if seq else 1)
         hp = host.data_ptr() + b0 * (T if seq else 1) * H * head
-        _lib.check(lib.gdn2_copy_heads(hp, devt.data_ptr(), rows, H, h0, Hs, head, int(to_device),
+        _lib.check(lib.gdn2_copy_heads(hp, devt.data_ptr(), rows, H, h0, hs, head, int(to_device),
                                        stream.cuda_stream), "gdn2_copy_heads")
 
     for s in range(nsh):
         sl = slots[s % nslot]
-        b0, h0s = (s // nhg) * Bs, (s % nhg) * Hs
+        b0, h0s, hs = plan[s]
+        ps = preps[hs]
         if s >= nslot:
             s_in.wait_event(sl.computed)        # the kernels of shard s - nslot read these
         for dst, src in zip(sl.x, xs):
-            copy(src, dst, b0, h0s, True, True, s_in)
+            copy(src, dst, b0, h0s, hs, True, True, s_in)
         if bwd:
-            copy(do_h, sl.do, b0, h0s, True, True, s_in)
+            copy(do_h, sl.do, b0, h0s, hs, True, True, s_in)
             if dhf_h is None:
                 with torch.cuda.stream(s_in):
                     sl.dhf.zero_()
             else:
-                copy(dhf_h, sl.dhf, b0, h0s, False, True, s_in)
+                copy(dhf_h, sl.dhf, b0, h0s, hs, False, True, s_in)
         if sl.h0 is not None:
-            copy(h0_h, sl.h0, b0, h0s, False, True, s_in)
+            copy(h0_h, sl.h0, b0, h0s, hs, False, True, s_in)
         sl.loaded.record(s_in)
         s_run = s_runs[s % nslot]
         s_run.wait_event(sl.loaded)
         if s >= nslot:
             s_run.wait_event(sl.drained)            # outputs of shard s - nslot copied out
-        _run(p, lib, p.code, sl.x, sl.h0, sl.do, sl.dhf, sl.o, sl.hf, sl.g, sl.dh0, sl.ws, Bs,
+        _run(ps, lib, ps.code, sl.x, sl.h0, sl.do, sl.dhf, sl.o, sl.hf, sl.g, sl.dh0, sl.ws, Bs,
              s_run.cuda_stream)
         with torch.cuda.stream(s_run):
             off = (sl.ws.data_ptr() + 255) // 256 * 256 - sl.ws.data_ptr()
             status_h[s].copy_(sl.ws[off:off + 20].view(torch.int32), non_blocking=True)
         sl.computed.record(s_run)
         s_out.wait_event(sl.computed)
-        copy(o_h, sl.o, b0, h0s, True, False, s_out)
-        copy(hf_h, sl.hf, b0, h0s, False, False, s_out)
+        copy(o_h, sl.o, b0, h0s, hs, True, False, s_out)
+        copy(hf_h, sl.hf, b0, h0s, hs, False, False, s_out)
         for dst, src in zip(g_h, sl.g):
-            copy(dst, src, b0, h0s, True, False, s_out)
+            copy(dst, src, b0, h0s, hs, True, False, s_out)
         if bwd:
-            copy(dh0_h, sl.dh0, b0, h0s, False, False, s_out)
+            copy(dh0_h, sl.dh0, b0, h0s, hs, False, False, s_out)
         sl.drained.record(s_out)
     s_out.synchronize()
     for st in s_runs:

@@ -365,7 +365,7 @@ def test_config4_forward_with_state():
 
 @pytest.mark.parametrize("dtype,backward", [(torch.float32, True), (torch.bfloat16, True),
                                             (torch.float32, False)])
-@pytest.mark.parametrize("shard,heads", [(1, 1), (1, 2), (5, 1), (1, None)])
+@pytest.mark.parametrize("shard,heads", [(1, 1), (1, 2), (5, 1), (1, None), (1, 4)])
 def test_streamed_host_batches_equal_device_call(dtype, backward, shard, heads):
     """gdn2_fwd_bwd on host tensors ((batch rows x head group) shards moved
     by pitched copies through a ring of device buffers) gives the same bits
