@@ -132,6 +132,8 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   const float* dhn = (c + 1 < p.nc) ? ws.dh + (chunk + 1) * D * D : dh_final + bh * D * D;
   float *pdq = ws.pdq + chunk * C * D, *pdk = ws.pdk + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
+  GDN2_TDECL;
+  GDN2_TMARK(0);
   const uint32_t tmem = setup(&ts);
   Ring ring = ring_of(sm, &ts, 2);
   int g = 0;
@@ -148,17 +150,26 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     });
   }
   drain(&ts.done, ph, ws.status);
+  GDN2_TMARK(1);
   {
     const float* dvp = ws.dvp + chunk * C * D;
     float* dv = ws.dv + chunk * C * D;
-    for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
-      float hv[16], lv[16];
-      float4 av[4];   // loads first: the dv stores below may alias them for the compiler
+    // every dv_partial load of this thread (its row, 64 columns) before the
+    // first dv store, which the compiler must assume may alias them
+    const int warp = threadIdx.x >> 5;
+    const int row = 32 * (warp & 3) + (threadIdx.x & 31), cb = (warp >> 2) * 64;
+    float4 avs[16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) av[k] = *reinterpret_cast<const float4*>(dvp + i * D + c0 + 4 * k);
+    for (int k = 0; k < 16; ++k) avs[k] = *reinterpret_cast<const float4*>(dvp + row * D + cb + 4 * k);
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      const int i = row, c0 = cb + 16 * grp;
+      float x[16];
+      tmem_ld16(lane_quarter_addr(tmem, c0), x);
+      float hv[16], lv[16];
 #pragma unroll
       for (int k = 0; k < 16; k += 4) {
-        const float4 a = av[k / 4];
+        const float4 a = avs[grp * 4 + k / 4];
         const float4 y = make_float4(san(a.x + x[k], p.clip), san(a.y + x[k + 1], p.clip),
                                      san(a.z + x[k + 2], p.clip), san(a.w + x[k + 3], p.clip));
         *reinterpret_cast<float4*>(dv + i * D + c0 + k) = y;
@@ -169,12 +180,13 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
       }
       tmem_st16(lane_quarter_addr(tmem, 256 + c0), hv);   // -dv: A operand (rows i, K = v)
       tmem_st16(lane_quarter_addr(tmem, 384 + c0), lv);
-    });
+    }
     tmem_st_wait();
   }
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  GDN2_TMARK(2);
   // contraction over the value dim v for every product
   {
     const Src srcs[2] = {direct(doc, rs), direct(hpre, D)};  // (i,v) (dk,v)
@@ -185,6 +197,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     });
   }
   drain(&ts.done, ph, ws.status);   // TMEM 256..511 free again
+  GDN2_TMARK(3);
   ring.nop = 3;
   {
     const Src srcs[3] = {direct(vnew, D), direct(doc, rs), direct(dhn, D)};  // (i|j,v) (i,v) (dk,v)
@@ -194,6 +207,7 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     });
   }
   drain(&ts.done, ph, ws.status);
+  GDN2_TMARK(4);
   float* t0 = sm;                  // the ring is free: two padded 128 x 128 tiles
   float* t1 = sm + TILE_FLOATS;
   float* dwp = ws.dWp + chunk * C * D;
@@ -204,27 +218,49 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
   acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
   acc_to_smem<false>(tmem, 256, t1);   // dkg
   __syncthreads();
+  GDN2_TMARK(5);
   // pdq = dqg e^gc; pdk = dkg e^{gc_last - gc}; pdgc = dqg q e^gc - dkg kg;
   // column sums of dkg kg
   const float* gl = gc + (C - 1) * D;
   float cs[4] = {0.f, 0.f, 0.f, 0.f};
-  for_tile([&](int i, int d) {
-    const float4 x = lds4(t0 + i * TLD + d), y = lds4(t1 + i * TLD + d);
-    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gl + d);
-    const float4 eg = exp4(g4);
-    const float4 qv = ld4<T>(qc + i * rs + d), kv = ld4<T>(kc + i * rs + d);
-    const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
-    st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
-        san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
-    const float4 pg = make_float4(dqg.x * (qv.x * eg.x), dqg.y * (qv.y * eg.y),
-                                  dqg.z * (qv.z * eg.z), dqg.w * (qv.w * eg.w));
-    const float4 f = exp4(make_float4(l4.x - g4.x, l4.y - g4.y, l4.z - g4.z, l4.w - g4.w));
-    const float4 xs = make_float4(y.x * (kv.x * f.x), y.y * (kv.y * f.y), y.z * (kv.z * f.z),
-                                  y.w * (kv.w * f.w));
-    st4(pdk + i * D + d, y.x * f.x, y.y * f.y, y.z * f.z, y.w * f.w);
-    st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
-    cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
-  });
+  // the for_tile walk (row i = warp + 8 it, columns d = 4 lane), four rows at
+  // a time with all their global loads issued before any store: the stores
+  // may alias the loads for the compiler, which would otherwise serialise
+  // one memory latency per row
+  {
+    const int d = (threadIdx.x & 31) * 4;
+    const float4 l4 = ldg4(gl + d);
+#pragma unroll 1
+    for (int it0 = 0; it0 < 16; it0 += 4) {
+      float4 g4[4], qv[4], kv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = (threadIdx.x >> 5) + 8 * (it0 + u);
+        g4[u] = ldg4(gc + i * D + d);
+        qv[u] = ld4<T>(qc + i * rs + d);
+        kv[u] = ld4<T>(kc + i * rs + d);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = (threadIdx.x >> 5) + 8 * (it0 + u);
+        const float4 x = lds4(t0 + i * TLD + d), y = lds4(t1 + i * TLD + d);
+        const float4 eg = exp4(g4[u]);
+        const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
+        st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
+            san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
+        const float4 q4 = qv[u], k4 = kv[u], gg = g4[u];
+        const float4 pg = make_float4(dqg.x * (q4.x * eg.x), dqg.y * (q4.y * eg.y),
+                                      dqg.z * (q4.z * eg.z), dqg.w * (q4.w * eg.w));
+        const float4 f = exp4(make_float4(l4.x - gg.x, l4.y - gg.y, l4.z - gg.z, l4.w - gg.w));
+        const float4 xs = make_float4(y.x * (k4.x * f.x), y.y * (k4.y * f.y), y.z * (k4.z * f.z),
+                                      y.w * (k4.w * f.w));
+        st4(pdk + i * D + d, y.x * f.x, y.y * f.y, y.z * f.z, y.w * f.w);
+        st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
+        cs[0] += xs.x; cs[1] += xs.y; cs[2] += xs.z; cs[3] += xs.w;
+      }
+    }
+  }
+  GDN2_TMARK(6);
   float* daqkT = ws.dAqkT + chunk * C * C;
   for_acc<128>(tmem, 384, [&](int i, int c, const float* v) {   // dAqk^T, coalesced per column
 #pragma unroll
@@ -258,7 +294,10 @@ k_tc_bwd_intra1(const T* __restrict__ q, const T* __restrict__ k, const float* _
     for (int r = 0; r < 8; ++r) csum += ts.colpart[r][d];   // fixed order
     pdgc[(C - 1) * D + d] += csum + __expf(gl[d]) * sdot;
   }
+  GDN2_TMARK(7);
   teardown(tmem);
+  GDN2_TMARK(8);
+  GDN2_TPRINT("bwd_intra1", 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -473,27 +512,49 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
   __syncthreads();
   float *pdk = ws.pdk + chunk * C * D, *pdb = ws.pdb + chunk * C * D,
         *pdgc = ws.pdgc + chunk * C * D;
-  for_tile([&](int j, int d) {
-    const float4 x = lds4(t0 + j * TLD + d);
-    const float4 eg = exp4(ldg4(gc + j * D + d));
-    const float4 kv = ld4<T>(kc + j * rs + d), bv = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
-    const float4 pk = ldg4(pdk + j * D + d), pg = ldg4(pdgc + j * D + d);
-    st4(pdk + j * D + d, san(pk.x + x.x * eg.x * bv.x, p.clip), san(pk.y + x.y * eg.y * bv.y, p.clip),
-        san(pk.z + x.z * eg.z * bv.z, p.clip), san(pk.w + x.w * eg.w * bv.w, p.clip));
-    st4(pdb + j * D + d, san(x.x * eg.x * kv.x, p.clip), san(x.y * eg.y * kv.y, p.clip),
-        san(x.z * eg.z * kv.z, p.clip), san(x.w * eg.w * kv.w, p.clip));
-    st4(pdgc + j * D + d, san(pg.x + x.x * (bv.x * kv.x * eg.x), p.clip),
-        san(pg.y + x.y * (bv.y * kv.y * eg.y), p.clip), san(pg.z + x.z * (bv.z * kv.z * eg.z), p.clip),
-        san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
-    // dwv -> dw, dv (same pass: more independent loads in flight)
-    const float4 y = lds4(t1 + j * TLD + d);
-    const float4 vv = ld4<T>(vc + j * rs + d), wv = ld4_gate<T>(wc + j * rs + d, GATES, kGateW);
-    const float4 dw = make_float4(y.x * vv.x, y.y * vv.y, y.z * vv.z, y.w * vv.w);
-    const float4 dvv = make_float4(y.x * wv.x, y.y * wv.y, y.z * wv.z, y.w * wv.w);
-    const float4 dwo = san4(san4(dw, p.clip), kFinalClipTc);
-    st4<T>(dw_out + off + j * rs + d, GATES ? mul4(dwo, sig_grad4(wv)) : dwo);
-    st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
-  });
+  // the for_tile walk (row j = warp + 8 it, columns d = 4 lane), two rows at
+  // a time with all their global loads issued before any store (the stores
+  // may alias the loads for the compiler, which would otherwise serialise
+  // the latencies); dwv -> dw, dv in the same pass
+  {
+    const int d = (threadIdx.x & 31) * 4;
+#pragma unroll 1
+    for (int it0 = 0; it0 < 16; it0 += 2) {
+      float4 gx[2], kx[2], bx[2], pkx[2], pgx[2], vx[2], wx[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int j = (threadIdx.x >> 5) + 8 * (it0 + u);
+        gx[u] = ldg4(gc + j * D + d);
+        kx[u] = ld4<T>(kc + j * rs + d);
+        bx[u] = ld4_gate<T>(bc + j * rs + d, GATES, kGateB);
+        pkx[u] = ldg4(pdk + j * D + d);
+        pgx[u] = ldg4(pdgc + j * D + d);
+        vx[u] = ld4<T>(vc + j * rs + d);
+        wx[u] = ld4_gate<T>(wc + j * rs + d, GATES, kGateW);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int j = (threadIdx.x >> 5) + 8 * (it0 + u);
+        const float4 x = lds4(t0 + j * TLD + d);
+        const float4 eg = exp4(gx[u]);
+        const float4 kv = kx[u], bv = bx[u], pk = pkx[u], pg = pgx[u];
+        st4(pdk + j * D + d, san(pk.x + x.x * eg.x * bv.x, p.clip), san(pk.y + x.y * eg.y * bv.y, p.clip),
+            san(pk.z + x.z * eg.z * bv.z, p.clip), san(pk.w + x.w * eg.w * bv.w, p.clip));
+        st4(pdb + j * D + d, san(x.x * eg.x * kv.x, p.clip), san(x.y * eg.y * kv.y, p.clip),
+            san(x.z * eg.z * kv.z, p.clip), san(x.w * eg.w * kv.w, p.clip));
+        st4(pdgc + j * D + d, san(pg.x + x.x * (bv.x * kv.x * eg.x), p.clip),
+            san(pg.y + x.y * (bv.y * kv.y * eg.y), p.clip), san(pg.z + x.z * (bv.z * kv.z * eg.z), p.clip),
+            san(pg.w + x.w * (bv.w * kv.w * eg.w), p.clip));
+        const float4 y = lds4(t1 + j * TLD + d);
+        const float4 vv = vx[u], wv = wx[u];
+        const float4 dw = make_float4(y.x * vv.x, y.y * vv.y, y.z * vv.z, y.w * vv.w);
+        const float4 dvv = make_float4(y.x * wv.x, y.y * wv.y, y.z * wv.z, y.w * wv.w);
+        const float4 dwo = san4(san4(dw, p.clip), kFinalClipTc);
+        st4<T>(dw_out + off + j * rs + d, GATES ? mul4(dwo, sig_grad4(wv)) : dwo);
+        st4<T>(dv_out + off + j * rs + d, san4(san4(dvv, p.clip), kFinalClipTc));
+      }
+    }
+  }
   fence_before_sync();
   __syncthreads();   // staging tiles and TMEM 0..255 free again
   fence_after_sync();
