@@ -351,19 +351,26 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
   }
   drain(&ts.done, ph, ws.status);
   {
+    // every dv_partial load of this thread before the first dv store
     const float* dvp = ws.dvp + chunk * C * D;
-    for_acc<128>(tmem, 0, [&](int i, int c0, const float* x) {
-      float4 av[4];   // loads first: the dv stores below may alias them for the compiler
+    const int warp = threadIdx.x >> 5;
+    const int i = 32 * (warp & 3) + (threadIdx.x & 31), cb = (warp >> 2) * 64;
+    float4 avs[16];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) av[kk] = *reinterpret_cast<const float4*>(dvp + i * D + c0 + 4 * kk);
+    for (int kk = 0; kk < 16; ++kk) avs[kk] = *reinterpret_cast<const float4*>(dvp + i * D + cb + 4 * kk);
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      const int c0 = cb + 16 * grp;
+      float x[16];
+      tmem_ld16(lane_quarter_addr(tmem, c0), x);
 #pragma unroll
       for (int kk = 0; kk < 16; kk += 4) {
-        const float4 a = av[kk / 4];
+        const float4 a = avs[grp * 4 + kk / 4];
         *reinterpret_cast<float4*>(dv + i * D + c0 + kk) =
             make_float4(san(a.x + x[kk], p.clip), san(a.y + x[kk + 1], p.clip),
                         san(a.z + x[kk + 2], p.clip), san(a.w + x[kk + 3], p.clip));
       }
-    });
+    }
   }
   fence_before_sync();
   __syncthreads();   // dv in global memory for the staging below; TMEM 0 free
@@ -401,13 +408,29 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
   acc_to_smem<false>(tmem, 0, t0);     // dqg / scale
   acc_to_smem<false>(tmem, 256, t1);   // dkg
   __syncthreads();
-  float cs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for_tile([&](int i, int d) {
-    const int hf = i / R;
+  float4 cs0 = make_float4(0.f, 0.f, 0.f, 0.f), cs1 = cs0;   // column sums per chunk
+  // the for_tile walk (row i = warp + 8 it, columns d = 4 lane), four rows at
+  // a time with their global loads before any store (see k_tc_bwd_intra1)
+  const int d = (threadIdx.x & 31) * 4;
+  const float4 l4a = ldg4(gc + (R - 1) * D + d), l4b = ldg4(gc + (2 * R - 1) * D + d);
+#pragma unroll 1
+  for (int it0 = 0; it0 < 16; it0 += 4) {
+  float4 g4v[4], qvv[4], kvv[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = (threadIdx.x >> 5) + 8 * (it0 + u);
+    g4v[u] = ldg4(gc + i * D + d);
+    qvv[u] = ld4<T>(qc + i * rs + d);
+    kvv[u] = ld4<T>(kc + i * rs + d);
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = (threadIdx.x >> 5) + 8 * (it0 + u);
+    const bool hf = i >= R;   // the tile's second chunk
     const float4 x = lds4(t0 + i * TLD + d), y = lds4(t1 + i * TLD + d);
-    const float4 g4 = ldg4(gc + i * D + d), l4 = ldg4(gc + (hf * R + R - 1) * D + d);
+    const float4 g4 = g4v[u], l4 = hf ? l4b : l4a;
     const float4 eg = exp4(g4);
-    const float4 qv = ld4<T>(qc + i * rs + d), kv = ld4<T>(kc + i * rs + d);
+    const float4 qv = qvv[u], kv = kvv[u];
     const float4 dqg = make_float4(p.scale * x.x, p.scale * x.y, p.scale * x.z, p.scale * x.w);
     st4(pdq + i * D + d, san(dqg.x * eg.x, p.clip), san(dqg.y * eg.y, p.clip),
         san(dqg.z * eg.z, p.clip), san(dqg.w * eg.w, p.clip));
@@ -418,19 +441,18 @@ k_tc_bwd_intra1_pair(const T* __restrict__ q, const T* __restrict__ k,
                                   y.w * (kv.w * f.w));
     st4(pdk + i * D + d, y.x * f.x, y.y * f.y, y.z * f.z, y.w * f.w);
     st4(pdgc + i * D + d, pg.x - xs.x, pg.y - xs.y, pg.z - xs.z, pg.w - xs.w);
-    cs[hf][0] += xs.x; cs[hf][1] += xs.y; cs[hf][2] += xs.z; cs[hf][3] += xs.w;
-  });
+    if (hf) { cs1.x += xs.x; cs1.y += xs.y; cs1.z += xs.z; cs1.w += xs.w; }
+    else { cs0.x += xs.x; cs0.y += xs.y; cs0.z += xs.z; cs0.w += xs.w; }
+  }
+  }
   float* daqkT = ws.dAqkT + chunk * C * C;
   for_acc<128>(tmem, 384, [&](int i, int c0, const float* v) {   // dAqk^T, coalesced per column
 #pragma unroll
     for (int t = 0; t < 16; ++t)
       daqkT[(c0 + t) * C + i] = (c0 + t <= i && (c0 + t) / R == i / R) ? san(v[t], p.clip) : 0.f;
   });
-  {
-    const int d = (threadIdx.x & 31) * 4;
-    st4(&ts.colpart[threadIdx.x >> 5][d], cs[0][0], cs[0][1], cs[0][2], cs[0][3]);
-    st4(&ts.colpart1[threadIdx.x >> 5][d], cs[1][0], cs[1][1], cs[1][2], cs[1][3]);
-  }
+  st4(&ts.colpart[threadIdx.x >> 5][d], cs0.x, cs0.y, cs0.z, cs0.w);
+  st4(&ts.colpart1[threadIdx.x >> 5][d], cs1.x, cs1.y, cs1.z, cs1.w);
   // rowdot[d] = sum_v dh_next(d, v) h_pre(d, v) of each chunk
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
