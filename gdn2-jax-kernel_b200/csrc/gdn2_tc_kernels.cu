@@ -374,22 +374,32 @@ k_tc_fwd_out(Problem p, Workspace ws, float* __restrict__ o) {
   const float* u = ws.U + chunk * C * D;
   float* vn = ws.vnew + chunk * C * D;
   float* vt = sm;
-  for_acc<128>(tmem, 0, [&](int v, int c0, const float* x) {
-    float* hi = vt + (c0 / KS) * 2 * SLICE_FLOATS;
-    float uu[16];   // all 16 loads issued before the stores to vnew (which may alias)
+  {
+    // all 64 U loads of this thread (its value column v, 64 rows i) before
+    // the first vnew store, which the compiler must assume may alias them
+    const int warp = threadIdx.x >> 5;
+    const int v = 32 * (warp & 3) + (threadIdx.x & 31), cb = (warp >> 2) * 64;
+    float uu[64];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) uu[t] = u[(c0 + t) * D + v];
+    for (int t = 0; t < 64; ++t) uu[t] = u[(cb + t) * D + v];
 #pragma unroll
-    for (int j = 0; j < 16; j += 4) {
-      float y[4];
+    for (int grp = 0; grp < 4; ++grp) {
+      const int c0 = cb + 16 * grp;
+      float x[16];
+      tmem_ld16(lane_quarter_addr(tmem, c0), x);
+      float* hi = vt + (c0 / KS) * 2 * SLICE_FLOATS;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        y[t] = uu[j + t] - x[j + t];
-        vn[(c0 + j + t) * D + v] = y[t];
+      for (int j = 0; j < 16; j += 4) {
+        float y[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          y[t] = uu[16 * grp + j + t] - x[j + t];
+          vn[(c0 + j + t) * D + v] = y[t];
+        }
+        st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + j, KS, make_float4(y[0], y[1], y[2], y[3]));
       }
-      st_split4(hi, hi + SLICE_FLOATS, v, c0 % KS + j, KS, make_float4(y[0], y[1], y[2], y[3]));
     }
-  });
+  }
   const float* aqkt = ws.AqkT + chunk * C * C;
   ring.base = sm + 4 * 2 * SLICE_FLOATS;
   ring.nop = 1;
