@@ -755,9 +755,9 @@ __device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Fra
 // Backward of the chunk scores (B4, gdn2_bwd.py:248-339), the in-chunk
 // reverse cumsum (B5, gdn2_bwd.py:32-41) and the final assembly with the
 // +-1e4 sanitiser (gdn2_pipeline.py:117-135); same contract as k_bwd_intra3.
-// The four pair sums run as four passes of products 128 x 128 x JW, one per
-// JW-wide block with its own reference row r (JW = 64, or 32 when a 64-row
-// spread of gc exceeds 80):
+// The four pair sums run as three passes of products 128 x 128 x JW (the two
+// dR sums accumulate in one), one per JW-wide block with its own reference
+// row r (JW = 64, or 32 when a 64-row spread of gc exceeds 80):
 //   dL_i = sum_J e^{gc_i - gc_rJ} sum_{j in J} dM_ij (k_j e^{gc_rJ - gc_j})
 //   dR_j = sum_I e^{gc_rI - gc_j} sum_{i in I} dM_ij (L_i e^{gc_i - gc_rI})
 // (every factor bounded for g <= 0 and a 32-row gc spread <= 80, otherwise
@@ -862,13 +862,17 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     // when the sum of the absolute block partials stays below CLIP (the JW
     // blocks nest in the BC blocks, so every reference prefix is a sum of
     // them).  Per thread: the largest such sum of each accumulator.
-    float gq_dq = 0.f, gq_dbk = 0.f, gq_dk2 = 0.f, gq_dk3 = 0.f;
-    float gg0 = 0.f, gg1 = 0.f, gg2 = 0.f, gg3 = 0.f;   // dgc terms of each pass
+    // Three passes: dL of the q scores, dL of the k scores, and the two dR
+    // sums in one accumulation (slices 0-3 from dAqk with scale q, 4-7 from
+    // dAkk with b k): only dRq + dRk is ever used, and the reference adds
+    // exactly that sum to dk per pair (gdn2_bwd.py:326), so the guard on the
+    // combined partials bounds its prefixes too.
+    float gq_dq = 0.f, gq_dbk = 0.f, gq_dk = 0.f;
+    float gg0 = 0.f, gg1 = 0.f, gg2 = 0.f;   // dgc terms of each pass
 #pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
+    for (int pass = 0; pass < 3; ++pass) {
       if (pass > 0) GDN2_TMARK(1 + 2 * pass);
       const bool left = pass < 2;                          // dL (row i) or dR (row j)
-      const float* MT = (pass == 0 || pass == 2) ? dAqkT : dAkkT;
       // Every global load of a slice is issued first (one memory latency per
       // slice), and the MMAs of slice sl are issued during slice sl+1 while
       // its loads are in flight: the issuing thread blocks for about as long
@@ -878,14 +882,16 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       const int e = threadIdx.x;
       const int rb = (e & 7) + ((e >> 5) & 3) * 8, kb = ((e >> 3) & 3) + (e >> 7) * 4;
       const int d0 = rb * 4;   // this thread's 4 x 4 block of the second operand
-      auto load_slice = [&](int k0, Frag& fm, Frag& fx) {
+      // kpart: this slice belongs to the k scores (pass 1, second half of 2)
+      auto load_slice = [&](int k0, bool kpart, Frag& fm, Frag& fx) {
+        const float* MT = kpart ? dAkkT : dAqkT;
         if (left) {
           load_trans(fm, MT, C, k0);                      // (i, jj) = dM(i, k0+jj)
 #pragma unroll
           for (int j = 0; j < 4; ++j) fx.v[j] = ld4<T>(kc + (k0 + kb * 4 + j) * rs + d0);
         } else {
           load_direct(fm, MT, C, k0);                     // (j, ii) = dM(k0+ii, j)
-          const T* src = pass == 2 ? qc : kc;
+          const T* src = kpart ? kc : qc;
 #pragma unroll
           for (int j = 0; j < 4; ++j) fx.v[j] = ld4<T>(src + (k0 + kb * 4 + j) * rs + d0);
         }
@@ -893,21 +899,24 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       Frag fm, fx;
       int pend_buf = -1, pend_J = 0;
       bool pend_acc = false;
+      const int nsl = left ? 4 : 8;
 #pragma unroll 1
-      for (int sl = 0; sl < 4; ++sl, ++gs) {
-        const int J = sl * 32 / JW, r = JW * J, k0 = 32 * sl;   // K slice k0 of block J
+      for (int sl = 0; sl < nsl; ++sl, ++gs) {
+        const int sl4 = sl & 3;
+        const bool kpart = pass == 1 || sl >= 4;
+        const int J = sl4 * 32 / JW, r = JW * J, k0 = 32 * sl4;   // K slice k0 of block J
         const int buf = gs & 1;
         GDN2_TSUB(0);
         ring_acquire(ring, buf, gs >> 1, ws.status);
         GDN2_TSUB(1);
-        load_slice(k0, fm, fx);
-        Frag fb;   // the gate of pass 3
-        if (pass == 3) {
+        load_slice(k0, kpart, fm, fx);
+        Frag fb;   // the gate of the right pass's k part
+        if (!left && kpart) {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             fb.v[j] = ld4_gate<T>(bc + (k0 + kb * 4 + j) * rs + d0, GATES, kGateB);
         }
-        if (crude) gather_stats(pass, k0 + kb * 4, d0, fm, fx, fb, p.scale, gst);
+        if (crude) gather_stats(left ? pass : (kpart ? 3 : 2), k0 + kb * 4, d0, fm, fx, fb, p.scale, gst);
         if (threadIdx.x == 0 && pend_buf >= 0) {
           mma3(tmem + 128 * pend_J, ring.op(pend_buf, 0), ring.op(pend_buf, 1), 128, KS / 8, pend_acc);
           commit(&ring.bars[pend_buf]);
@@ -928,7 +937,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           for (int j = 0; j < 4; ++j) {   // (d, ii) = L = l_i e^{gc_i - gc_r}
             const float4 gi = ldg4(gc + (k0 + kb * 4 + j) * GLD + d0);
             float4 lv = fx.v[j];
-            if (pass == 2) {
+            if (!kpart) {
               lv = scl(lv, p.scale);
             } else {
               const float4 bv = fb.v[j];
@@ -944,7 +953,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         GDN2_TSUB(3);
         pend_buf = buf;
         pend_J = J;
-        pend_acc = k0 > r;
+        pend_acc = k0 > r || sl >= 4;   // the k part adds onto the q part's blocks
       }
       if (threadIdx.x == 0) {
         mma3(tmem + 128 * pend_J, ring.op(pend_buf, 0), ring.op(pend_buf, 1), 128, KS / 8, pend_acc);
@@ -1045,16 +1054,11 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
             for (int u = 0; u < 4; ++u) {
               dkr[qd * 16 + t + u] += val[t + u];
               dgr[qd * 16 + t + u] -= kv[u] * val[t + u];
-              if (pass == 2) {
-                gq_dk2 = fmaxf(gq_dk2, sab[t + u]);
-                gg2 = fmaxf(gg2, fabsf(kv[u]) * sab[t + u]);
-              } else {
-                gq_dk3 = fmaxf(gq_dk3, sab[t + u]);
-                gg3 = fmaxf(gg3, fabsf(kv[u]) * sab[t + u]);
-              }
+              gq_dk = fmaxf(gq_dk, sab[t + u]);
+              gg2 = fmaxf(gg2, fabsf(kv[u]) * sab[t + u]);
             }
           }
-          if (pass == 3) {
+          {
             float4 pkv[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t) pkv[t] = ldg4(pdk + x * D + c0 + 4 * t);
@@ -1076,7 +1080,7 @@ k_tc_bwd_intra3(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     GDN2_TMARK(9);
     bool bad;
     if (!crude) {
-      bad = !(gq_dq < lim && gq_dbk < lim && gq_dk2 + gq_dk3 < lim && gg0 + gg1 + gg2 + gg3 < lim);
+      bad = !(gq_dq < lim && gq_dbk < lim && gq_dk < lim && gg0 + gg1 + gg2 < lim);
     } else {
       __syncthreads();   // the statistics of every thread are in
       const float rq = gstat[kRowQ][x], rk = gstat[kRowK][x];
