@@ -719,6 +719,10 @@ k_tc_bwd_intra2(const T* __restrict__ k, const T* __restrict__ v, const T* __res
 __device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Frag& fm,
                                              const Frag& fx, const Frag& fb, float scale,
                                              float* gst) {
+  // lane bits: 0-2 pick the row block (d0), 3-4 the column block (j0); the
+  // sums over lanes sharing a row (or column) block are formed with shuffles
+  // first, so one lane per group does the shared-memory atomic
+  const int lane = threadIdx.x & 31;
   auto amax = [](float* a, float v) {   // v >= 0 (or NaN, which the guard test rejects)
     atomicMax(reinterpret_cast<int*>(a), __float_as_int(v));
   };
@@ -731,10 +735,18 @@ __device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Fra
       const float4 v = fm.v[j];
       const float a = fabsf(v.x), b2 = fabsf(v.y), c2 = fabsf(v.z), d2 = fabsf(v.w);
       r[0] += a; r[1] += b2; r[2] += c2; r[3] += d2;
-      atomicAdd(coll + j0 + j, a + b2 + c2 + d2);
+      float cs = a + b2 + c2 + d2;   // column j0 + j: the 8 lanes of this column block
+      cs += __shfl_xor_sync(0xffffffffu, cs, 1);
+      cs += __shfl_xor_sync(0xffffffffu, cs, 2);
+      cs += __shfl_xor_sync(0xffffffffu, cs, 4);
+      if ((lane & 7) == 0) atomicAdd(coll + j0 + j, cs);
     }
 #pragma unroll
-    for (int t = 0; t < 4; ++t) atomicAdd(rowl + d0 + t, r[t]);
+    for (int t = 0; t < 4; ++t) {   // row d0 + t: the 4 lanes of this row block
+      r[t] += __shfl_xor_sync(0xffffffffu, r[t], 8);
+      r[t] += __shfl_xor_sync(0xffffffffu, r[t], 16);
+      if ((lane & 24) == 0) atomicAdd(rowl + d0 + t, r[t]);
+    }
   }
   if (pass == 1) return;
   float m[4] = {0.f, 0.f, 0.f, 0.f};
@@ -748,7 +760,14 @@ __device__ __forceinline__ void gather_stats(int pass, int j0, int d0, const Fra
   }
   float* mx = gst + (pass == 0 ? 4 : (pass == 2 ? 5 : 6)) * 128;
 #pragma unroll
-  for (int t = 0; t < 4; ++t) amax(mx + d0 + t, m[t]);
+  for (int t = 0; t < 4; ++t) {   // column d0 + t: the 4 lanes of this row block
+    // a NaN must survive the reduction (fmaxf would drop it): compare instead
+    float o = __shfl_xor_sync(0xffffffffu, m[t], 8);
+    m[t] = (o > m[t] || o != o) ? o : m[t];
+    o = __shfl_xor_sync(0xffffffffu, m[t], 16);
+    m[t] = (o > m[t] || o != o) ? o : m[t];
+    if ((lane & 24) == 0) amax(mx + d0 + t, m[t]);
+  }
 }
 
 // ---------------------------------------------------------------------------
