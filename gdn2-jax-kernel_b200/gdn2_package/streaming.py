@@ -64,6 +64,19 @@ def _run(p, lib, code, xs, h0, do, dhf, o, hf, grads, dh0, ws, Bs, stream):
     _lib.check(rc, "gdn2_bwd")
 
 
+def _shard_plan(B, H, Bs, Hs, edges):
+    """Shards (b0, h0, heads) in streaming order: batch rows of Bs by head
+    groups of Hs; with ``edges`` the first and the last group go as single
+    heads (the copy-in before the first kernels and the work after the last
+    copy-in are what the pipeline cannot overlap)."""
+    plan = [(bi * Bs, gi * Hs, Hs) for bi in range(B // Bs) for gi in range(H // Hs)]
+    if edges and Hs > 1 and len(plan) > 2:
+        first, last = plan[0], plan[-1]
+        plan = ([(first[0], first[1] + i, 1) for i in range(Hs)] + plan[1:-1]
+                + [(last[0], last[1] + i, 1) for i in range(Hs)])
+    return plan
+
+
 def _head_group(Bs, T, H, D=128):
     """Smallest head group whose shard still gives the chunk kernels one CTA
     per SM (148 on a B200): small shards shorten the copy-in of the first
@@ -149,11 +162,7 @@ def gdn2_fwd_bwd(q, k, v, w, b, g, scale, dout=None, dh_final=None, h0=None, sha
     o_h, hf_h, *g_h = out
     dh0_h = g_h.pop() if bwd else None
     nb, nhg = B // Bs, H // Hs
-    plan = [(bi * Bs, gi * Hs, Hs) for bi in range(nb) for gi in range(nhg)]   # (b0, h0, heads)
-    if edges and Hs > 1 and len(plan) > 2:
-        first, last = plan[0], plan[-1]
-        plan = ([(first[0], first[1] + i, 1) for i in range(Hs)] + plan[1:-1]
-                + [(last[0], last[1] + i, 1) for i in range(Hs)])
+    plan = _shard_plan(B, H, Bs, Hs, edges)
     preps = {hs: (p if hs == Hs else prepared(hs)) for hs in {x[2] for x in plan}}
     nsh = len(plan)
     nslot = max(1, min(int(depth), nsh))

@@ -135,6 +135,18 @@ def test_stage_functions_have_the_reference_names():
         gdn2_fwd.BT = 256
 
 
+def test_streamed_shard_plan_covers_every_head_once():
+    from gdn2_package.streaming import _shard_plan
+    for B, H, Bs, Hs, edges in [(8, 6, 1, 3, True), (8, 6, 1, 3, False), (4, 4, 2, 2, True),
+                                (1, 6, 1, 6, True), (2, 1, 1, 1, True)]:
+        plan = _shard_plan(B, H, Bs, Hs, edges)
+        cells = [(b, h) for b0, h0, hs in plan for b in range(b0, b0 + Bs) for h in range(h0, h0 + hs)]
+        assert sorted(cells) == [(b, h) for b in range(B) for h in range(H)], (B, H, Bs, Hs, edges)
+        if edges and Hs > 1 and B * H // (Bs * Hs) > 2:
+            assert plan[0][2] == 1 and plan[-1][2] == 1 and plan[Hs][2] == Hs
+    assert len(_shard_plan(8, 6, 1, 3, True)) == 16 - 2 + 6
+
+
 def test_streamed_head_group_fills_the_gpu():
     from gdn2_package.streaming import _head_group
     assert _head_group(1, 8192, 6) == 3      # 64 chunks x 3 heads >= 148 CTAs
