@@ -2,6 +2,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -27,7 +28,7 @@ struct Profiler {
 Profiler g_prof;
 std::mutex g_prof_mu;
 int g_diag = 0;   // per-stage diagnostics on (gdn2_diag_enable)
-int g_pair64 = 1;  // BT = 64 chunks paired into 128-row tensor-core tiles (gdn2_pair64_enable)
+std::atomic<int> g_pair64{1};  // BT = 64 chunks paired into 128-row tiles (gdn2_pair64_enable)
 
 void prof_hook(int stage, int end, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -209,9 +210,7 @@ int gdn2_diag_enable(int on) {
 }
 
 int gdn2_pair64_enable(int on) {
-  const int prev = g_pair64;
-  g_pair64 = on != 0;
-  return prev;
+  return g_pair64.exchange(on != 0 ? 1 : 0);
 }
 
 int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,

@@ -1,9 +1,10 @@
 // The reference's stage functions as separate entry points: Kernels A, B, C
 // and D of gdn2_fwd.py and B1-B5 of gdn2_bwd.py, each on the reference's
 // chunked layouts ((B, H, nc, BT, .) float32, gc_last (B, H, nc, D)).  The
-// fused pipeline (gdn2_fwd / gdn2_bwd) never calls these: they serve code
-// that composes the stages itself.  CUDA-core kernels, one CTA per chunk
-// (or per (b, h) and 32 value columns for the two serial scans), with every
+// fused kernels never call these: they serve code that composes the stages
+// itself, and the Python layer runs head dim 256 (which the fused kernels do
+// not cover) through them.  CUDA-core kernels, one CTA per chunk (or per
+// (b, h) and 32 value columns for the two serial scans), with every
 // sanitiser where the reference has it.
 #include <cstdio>
 

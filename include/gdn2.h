@@ -136,8 +136,9 @@ int gdn2_diag_enable(int on);
  * tile (block-diagonal chunk scores and WY solve, gates and gc_last per
  * chunk, one state step per chunk), the same function as the BT = 64
  * CUDA-core kernels.  Needs T % 128 == 0 (otherwise the CUDA-core kernels
- * run).  On by default; per call, GDN2_NO_PAIR opts out.  Returns the
- * previous setting. */
+ * run).  On by default; per call, GDN2_NO_PAIR opts out.  Process-wide: a
+ * forward that kept residuals and its backward must run under the same
+ * setting, so change it only between steps.  Returns the previous setting. */
 int gdn2_pair64_enable(int on);
 int gdn2_diag_read(const void* workspace, size_t workspace_bytes, void* stream, int n,
                    int* nonfinite, float* maxabs);
@@ -174,8 +175,9 @@ int gdn2_copy_heads(void* host, void* dev, long rows, int H, int h0, int Hs, siz
 
 /* The reference's stage functions as separate entry points, on its chunked
  * layouts: (B, H, nc, BT, .) float32 tiles, gc_last (B, H, nc, D), inputs
- * q..g (B, T, H, D) of `dtype` where named; BT 64, 128 or 256.  The fused gdn2_fwd / gdn2_bwd
- * never call them.  Each replaces the reference function of the same name:
+ * q..g (B, T, H, D) of `dtype` where named; BT 64, 128 or 256; D 64, 128 or
+ * 256 (D = 256 with BT <= 128).  The fused gdn2_fwd / gdn2_bwd never call
+ * them.  Each replaces the reference function of the same name:
  *   gdn2_stage_scores        build_chunk_scores_pallas (gdn2_fwd.py:142-170)
  *   gdn2_stage_wy_solve      wy_solve_pallas (gdn2_fwd.py:246-260), any BC;
  *                            BT = 256 needs BC <= 128 and n_chunks*BC*BC
