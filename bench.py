@@ -309,8 +309,25 @@ def run_ours(args, rank, world, local_rank):
     del inp
     scale = D ** -0.5
 
+    # --segments: the chunk-parallel scan of gdn2_package.segmented (every
+    # sequence cut into S time segments joined by their affine maps); 0 plans S
+    from gdn2_package import segmented as SG
+    S = args.segments
+    if S == 0:
+        S = SG.plan_segments(B, T, H, BT, torch.cuda.get_device_properties(dev).multi_processor_count)
+    if S > 1 and not (cfg["bwd"] and BT == 128 and D == 128):
+        raise SystemExit("--segments needs a fwd+bwd configuration with BT = D = 128")
+
     def step(d):
         h0 = d.get("h0")
+        if S > 1:
+            x = [d[n] for n in names]
+            r = SG.segmented_forward(*x, scale, h0, S)
+            grads = SG.segmented_backward(r[2], d["dout"], d["dh_final"]) if r else None
+            if grads is None:   # a sanitiser acted: the serial path
+                (o, h), res = gdn2_pipeline._gdn2_core_fwd(*x, scale, h0)
+                return o, h, gdn2_pipeline._gdn2_core_bwd(scale, res, (d["dout"], d["dh_final"]))
+            return r[0], r[1], grads
         if not cfg["bwd"]:
             p = gdn2_fwd._Prepared(*[d[n] for n in names], scale, h0)
             o, h, _ = gdn2_fwd._run_forward(p)
@@ -450,6 +467,7 @@ def run_ours(args, rank, world, local_rank):
                    "global_batch": B * world if H == cfg["H"] else B, "seq_len": T,
                    "heads": H, "head_dim": D,
                    "parallelism": f"dp{world} (batch x head shards, no collective)",
+                   "segments": S,
                    "l2": "inputs larger than L2"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
@@ -536,6 +554,9 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="override B (profiling of smaller cases only)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling: skip the host-buffer leg")
+    ap.add_argument("--segments", type=int, default=1,
+                    help="time segments per sequence for the chunk-parallel scan on one GPU "
+                         "(1 = serial scan, 0 = planned for this GPU; fwd+bwd, BT = D = 128)")
     ap.add_argument("--mode", default="dp", choices=["dp", "sp"],
                     help="dp: config 1 per GPU (default); sp: config 3 (B1 T131072 H8) split "
                          "over the GPUs by sequence")

@@ -14,3 +14,4 @@ from . import gdn2_fwd, gdn2_bwd, gdn2_pipeline  # noqa: E402,F401
 from . import sequence_parallel  # noqa: E402,F401
 from .gdn2_decode import gdn2_decode  # noqa: E402,F401
 from .streaming import gdn2_fwd_bwd  # noqa: E402,F401
+from .segmented import gdn2_segmented_forward_trainable  # noqa: E402,F401
