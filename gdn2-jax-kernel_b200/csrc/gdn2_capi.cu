@@ -63,7 +63,7 @@ int cuda_fail(cudaError_t e, const char* where) {
 }
 
 int validate(int dtype, int B, int T, int H, int D, int BT, int BC, float scale, float clip) {
-  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR);
+  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR | GDN2_NO_OUT);
   if (dtype != GDN2_F32 && dtype != GDN2_BF16)
     return fail(GDN2_ERR_INVALID, "unsupported dtype code %s%ld", "", dtype);
   if (B <= 0 || T <= 0 || H <= 0)
@@ -314,8 +314,11 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
              int D, int BT, int BC, float scale, float clip, void* stream) {
   int rc = validate(dtype, B, T, H, D, BT, BC, scale, clip);
   if (rc) return rc;
-  if (!q || !k || !v || !w || !b || !g || !o || !h_final || !workspace)
+  const bool no_out = (dtype & GDN2_NO_OUT) != 0;
+  if (!q || !k || !v || !w || !b || !g || (!o && !no_out) || !h_final || !workspace)
     return fail(GDN2_ERR_INVALID, "%snull buffer pointer");
+  if (no_out && (!use_tc(BT, D) || !save_residuals))
+    return fail(GDN2_ERR_INVALID, "%sGDN2_NO_OUT needs BT = D = 128 and save_residuals");
   const size_t need = gdn2_workspace_bytes(B, T, H, D, BT, 0);
   if (workspace_bytes < need)
     return fail(GDN2_ERR_WORKSPACE, "%sworkspace too small: need %ld bytes, got %ld", "",
@@ -325,7 +328,7 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
   Problem p = make_problem(B, T, H, D, KT, BC, scale, clip);
   p.sub = pair ? 2 : 1;
   p.gates = (dtype & GDN2_GATES_RAW) != 0;
-  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR);
+  dtype &= ~(GDN2_GATES_RAW | GDN2_NO_PAIR | GDN2_NO_OUT);
   const Workspace ws = Workspace::carve(workspace, B, H, p.nc, KT, D, false, p.sub);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = clear_status(ws, s))) return rc;
@@ -334,7 +337,7 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
            : run_fwd_intra<__nv_bfloat16>(KT, D, q, k, v, w, b, g, p, ws, s);
   if (rc) return rc;
   if (use_tc(KT, D)) {
-    cudaError_t e = launch_tc_fwd(p, ws, h0, o, h_final, s, hook());
+    cudaError_t e = launch_tc_fwd(p, ws, h0, o, h_final, s, hook(), !no_out);
     return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "tc_fwd");
   }
   return run_fwd_state(BT, D, p, ws, h0, o, h_final, save_residuals, s);
@@ -380,7 +383,10 @@ int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void*
     }
   }
   if (use_tc(KT, D)) {
-    cudaError_t e = launch_tc_bwd_state(p, ws, dout, dh_final, dh0, s, hook());
+    // residuals_valid == 2: the bwd_prep terms of this dout are in place
+    // (gdn2_sp_segment op 2 formed them from the same residuals)
+    cudaError_t e = launch_tc_bwd_state(p, ws, dout, dh_final, dh0, s, hook(),
+                                        residuals_valid != 2 || p.sub != 1);
     if (e != cudaSuccess) return cuda_fail(e, "tc_bwd_state");
   } else {
     rc = run_bwd_state(KT, D, p, ws, dout, dh_final, dh0, s);

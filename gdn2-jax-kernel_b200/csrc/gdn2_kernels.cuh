@@ -410,10 +410,13 @@ cudaError_t launch_tc_bwd_intra12(const T* q, const T* k, const T* v, const T* w
 cudaError_t launch_tc_sp(int op, const Problem& p, const Workspace& ws, const float* in, float* o,
                          float* out, cudaStream_t s, const LaunchHook& hook);
 // Tensor-core path (chunk = head dim = 128, float32 workspace), gdn2_tc_kernels.cu.
+// outputs = false: no k_tc_fwd_out (o and the vnew residual are left to a
+// later rescan); with_prep = false: the k_tc_bwd_prep terms are in place.
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,
-                          float* hfinal, cudaStream_t s, const LaunchHook& hook);
+                          float* hfinal, cudaStream_t s, const LaunchHook& hook,
+                          bool outputs = true);
 cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
                                 const float* dh_final, float* dh0, cudaStream_t s,
-                                const LaunchHook& hook);
+                                const LaunchHook& hook, bool with_prep = true);
 
 }  // namespace gdn2

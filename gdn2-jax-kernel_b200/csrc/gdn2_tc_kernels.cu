@@ -526,7 +526,7 @@ constexpr size_t kScan = (kScanSlots + 4) * (size_t)kScanSliceBytes;   // raw ri
 }  // namespace
 
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,
-                          float* hfinal, cudaStream_t s, const LaunchHook& hook) {
+                          float* hfinal, cudaStream_t s, const LaunchHook& hook, bool outputs) {
   cudaError_t e;
   const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
   auto affine = p.sub == 2 ? k_tc_affine<2> : k_tc_affine<1>;
@@ -542,6 +542,7 @@ cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0
   k_tc_scan<false><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, h0, hfinal);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   hook.end(kStageFwdScan, s);
+  if (!outputs) return cudaSuccess;
   hook.begin(kStageFwdOut, s);
   fwd_out<<<nchunks, kThreads, kRing3, s>>>(p, ws, o);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -551,16 +552,18 @@ cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0
 
 cudaError_t launch_tc_bwd_state(const Problem& p, const Workspace& ws, const float* dout,
                                 const float* dh_final, float* dh0, cudaStream_t s,
-                                const LaunchHook& hook) {
+                                const LaunchHook& hook, bool with_prep) {
   cudaError_t e;
   const unsigned nchunks = (unsigned)p.B * p.H * p.nc;
   auto bwd_prep = p.sub == 2 ? k_tc_bwd_prep<2> : k_tc_bwd_prep<1>;
   if ((e = prep(bwd_prep, kRing3)) != cudaSuccess) return e;
   if ((e = prep(k_tc_scan<true>, kScan)) != cudaSuccess) return e;
-  hook.begin(kStageBwdPrep, s);
-  bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, dout);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  hook.end(kStageBwdPrep, s);
+  if (with_prep) {
+    hook.begin(kStageBwdPrep, s);
+    bwd_prep<<<nchunks, kThreads, kRing3, s>>>(p, ws, dout);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    hook.end(kStageBwdPrep, s);
+  }
   hook.begin(kStageBwdScan, s);
   k_tc_scan<true><<<dim3(p.H, p.B), kThreads, kScan, s>>>(p, ws, dh_final, dh0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;

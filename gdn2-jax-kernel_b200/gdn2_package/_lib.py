@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libgdn2.so")
 F32, BF16 = 0, 1
 GATES_RAW = 0x100   # flag OR-ed into the dtype code (include/gdn2.h)
 NO_PAIR = 0x200     # flag: BT = 64 on the CUDA-core kernels for this call
+NO_OUT = 0x400      # flag: gdn2_fwd forms residuals and h_final, not o (a rescan follows)
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA = 0, -1, -2, -3
 # bits of gdn2_workspace_status (include/gdn2.h)
 STATUS_WAIT_TIMEOUT, STATUS_FWD_STATE_CLIPPED, STATUS_BWD_STATE_CLIPPED = 1, 2, 4

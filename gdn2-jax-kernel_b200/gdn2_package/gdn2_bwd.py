@@ -16,14 +16,16 @@ from . import gdn2_fwd as _fwd
 _FINAL_CLIP = 1e4  # gdn2_pipeline.py:34
 
 
-def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
+def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None, _prep_done=False):
     """Cotangents (dq, dk, dv, dw, db, dg, dh0) of (o, h_final) w.r.t. the
     inputs, as _gdn2_core_bwd returns them (gdn2_pipeline.py:70-137): final
     +-1e4 sanitiser, each gradient cast to its input's dtype.
 
     ``workspace`` may be the buffer a previous forward filled with residuals
     (``gdn2_pallas_forward_trainable`` does this) to skip the recompute of
-    the forward; without it the forward is recomputed as in the reference.
+    the forward; without it the forward is recomputed as in the reference.  ``_prep_done`` (internal:
+    sequence_parallel / segmented): a gdn2_sp_segment op 2 with this same
+    dout already formed the per-chunk backward terms in ``workspace``.
     """
     if _fwd._head_dim(q) in _fwd._STAGE_D:
         return _stage_backward(q, k, v, w, b, g, scale, h0, dout, dh_final)
@@ -49,7 +51,8 @@ def gdn2_backward(q, k, v, w, b, g, scale, h0, dout, dh_final, workspace=None):
         p.code, *p.ptrs(), p.h0.data_ptr() if p.h0 is not None else None, do.data_ptr(),
         dhf.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dw.data_ptr(),
         db.data_ptr(), dg.data_ptr(), dh0.data_ptr(), ws.data_ptr(), ws.numel(),
-        int(residuals_valid), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip, p.stream)
+        (2 if _prep_done else 1) if residuals_valid else 0, p.B, p.T, p.H, p.D, p.C, p.bc,
+        p.scale, p.clip, p.stream)
     _lib.check(rc, "gdn2_bwd")
     _lib.check_status(ws, p.stream, "gdn2_bwd", synced=p.on_host)
     out = [p.unpad(t) for t in (dq, dk, dv, dw, db, dg)]

@@ -210,14 +210,17 @@ class _Prepared:
         return torch.empty(n, dtype=torch.uint8, device=self.dev)
 
 
-def _run_forward(p, save_residuals=False, ws=None, debug_tag=""):
+def _run_forward(p, save_residuals=False, ws=None, debug_tag="", outputs=True):
+    """gdn2_fwd on prepared inputs.  outputs=False (BT = D = 128, residuals
+    kept): o is left unwritten for a gdn2_sp_segment op 1 rescan to form."""
     lib = _lib.load()
     lib.gdn2_diag_enable(int(_GDN2_FWD_DIAG))
     o = torch.empty((p.B, p.T, p.H, p.D), dtype=torch.float32, device=p.dev)
     h_final = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
     if ws is None:
         ws = p.workspace(save_residuals)
-    rc = lib.gdn2_fwd(p.code, *p.ptrs(), p.h0.data_ptr() if p.h0 is not None else None,
+    code = p.code | (0 if outputs else _lib.NO_OUT)
+    rc = lib.gdn2_fwd(code, *p.ptrs(), p.h0.data_ptr() if p.h0 is not None else None,
                       o.data_ptr(), h_final.data_ptr(), ws.data_ptr(), ws.numel(),
                       int(save_residuals), p.B, p.T, p.H, p.D, p.C, p.bc, p.scale, p.clip,
                       p.stream)

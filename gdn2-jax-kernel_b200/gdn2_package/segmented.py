@@ -35,10 +35,10 @@ def plan_segments(B, T, H, C, sms):
     """Segments per sequence: 1 (no split) unless the (batch, head) scans
     fill at most an eighth of the SMs; then the largest power of two S >= 2
     with B * H * S <= sms CTAs and segments of at least MIN_SEGMENT_CHUNKS
-    whole chunks.  (Measured on B200: config 3, 8 scans, 34.4 -> 26.5 ms per
+    whole chunks.  (Measured on B200: config 3, 8 scans, 34.4 -> 24.3 ms per
     fwd+bwd step with S = 16; config 1, 48 scans, 8.8 -> 10.7 ms with S = 2:
-    the joins cost about three passes of per-chunk work, more than the
-    shorter chains save once the scans already occupy a third of the SMs.)"""
+    the joins cost passes of per-chunk work that outweigh the shorter chains
+    once the scans already occupy a third of the SMs.)"""
     S = 1
     if B * H * 8 > sms:
         return S
@@ -121,7 +121,7 @@ def segmented_backward(state, dout, dh_final):
         torch.as_tensor(dh_final).to(p.dev, torch.float32)
     g_in, g0 = _compose_backward(state.maps, e, dhf, S)
     grads = _bwd.gdn2_backward(*p.t, p.scale, st.h_start, st.do, g_in.float().contiguous(),
-                               workspace=st.ws)
+                               workspace=st.ws, _prep_done=True)
     bits = st.bwd_bits | _lib.workspace_status(st.ws, p.stream)
     if bits & _lib.STATUS_WAIT_TIMEOUT:
         raise _lib.Gdn2Error("segmented backward: a bounded barrier wait inside a kernel timed out")

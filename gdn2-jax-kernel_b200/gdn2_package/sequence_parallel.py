@@ -125,7 +125,8 @@ def sp_forward_local(q, k, v, w, b, g, scale, rank):
     if p.T != p.T_user:
         raise _fwd.Gdn2ShapeError("sequence parallelism needs segments divisible by BT")
     ws = p.workspace(True)
-    o, c_seg, _ = _fwd._run_forward(p, save_residuals=True, ws=ws)
+    # o is formed by the rescan (op 1), not by this zero-state run
+    o, c_seg, _ = _fwd._run_forward(p, save_residuals=True, ws=ws, outputs=False)
     bits = _status(p, ws)
     P = torch.empty((p.B, p.H, p.D, p.D), dtype=torch.float32, device=p.dev)
     _seg(0, ws, p, None, None, P)
@@ -169,7 +170,8 @@ def sp_backward_finish(state, terms, dh_final=None):
         torch.as_tensor(dh_final).to(p.dev, torch.float32)
     g_in, g0 = compose_backward(state.maps, terms, dhf)
     g_rank = g_in[state.rank].float().contiguous()
-    grads = _bwd.gdn2_backward(*p.t, p.scale, state.h_start, state.do, g_rank, workspace=state.ws)
+    grads = _bwd.gdn2_backward(*p.t, p.scale, state.h_start, state.do, g_rank, workspace=state.ws,
+                               _prep_done=True)
     state.bwd_bits |= _status(p, state.ws)
     grads = [t.to(dt) for t, dt in zip(grads[:6], p.in_dtypes)]
     dh0 = torch.nan_to_num(g0.clamp(-1e4, 1e4), nan=0.0).float()

@@ -44,6 +44,12 @@ enum { GDN2_F32 = 0, GDN2_BF16 = 1 };
  * gdn2_pair64_enable() would pair chunks on the tensor cores (the forward
  * and the backward of one step must agree). */
 #define GDN2_NO_PAIR 0x200
+/* OR-ed into the dtype argument of gdn2_fwd (BT = D = 128 only, with
+ * save_residuals = 1): the call forms the residuals and h_final but not the
+ * chunk outputs, and `o` may be NULL.  For a segment whose outputs a
+ * gdn2_sp_segment op 1 rescan forms afterwards (sequence parallelism, the
+ * chunk-parallel scan on one GPU), which rewrites them in full. */
+#define GDN2_NO_OUT 0x400
 enum {
   GDN2_OK = 0,
   GDN2_ERR_INVALID = -1,   /* bad shape / argument (reference: AssertionError, gdn2_fwd.py:145-146) */
@@ -72,7 +78,9 @@ int gdn2_fwd(int dtype, const void* q, const void* k, const void* v, const void*
 /* Backward of the custom_vjp: replaces _gdn2_core_bwd (gdn2_pipeline.py:70-137;
  * B1-B5 at gdn2_bwd.py:32, 45, 99, 213, 342).  residuals_valid = 0 recomputes
  * the forward from the inputs exactly as the reference does; 1 reuses the
- * residuals a gdn2_fwd(save_residuals=1) call left in the same workspace.
+ * residuals a gdn2_fwd(save_residuals=1) call left in the same workspace; 2
+ * (BT = D = 128) also reuses the per-chunk backward terms of this same dout
+ * that a gdn2_sp_segment op 2 call left there after those residuals.
  * h0 may be NULL; dh_final must be given (zeros for no cotangent). */
 int gdn2_bwd(int dtype, const void* q, const void* k, const void* v, const void* w,
              const void* b, const void* g, const float* h0, const float* dout,

@@ -87,6 +87,28 @@ def test_status_bits_match_header():
     assert int(bits["B4_EXACT"]) == _lib.STATUS_B4_EXACT
 
 
+def test_dtype_flags_match_header():
+    src = open(os.path.join(ROOT, "include", "gdn2.h")).read()
+    flags = dict(re.findall(r"#define GDN2_(GATES_RAW|NO_PAIR|NO_OUT) (0x[0-9a-f]+)", src))
+    assert int(flags["GATES_RAW"], 16) == _lib.GATES_RAW
+    assert int(flags["NO_PAIR"], 16) == _lib.NO_PAIR
+    assert int(flags["NO_OUT"], 16) == _lib.NO_OUT
+
+
+def test_no_out_needs_the_tensor_core_path_without_gpu_work():
+    """GDN2_NO_OUT leaves o to a rescan that only the BT = D = 128 path has:
+    elsewhere (and without saved residuals) the call is refused before any
+    launch."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(256)
+    args = [fake] * 6 + [None, None, fake, fake, 1 << 30]
+    rc = lib.gdn2_fwd(_lib.F32 | _lib.NO_OUT, *args, 1, 1, 128, 2, 64, 64, 16, 0.1, 1e3, None)
+    assert rc == _lib.ERR_INVALID
+    assert "NO_OUT" in lib.gdn2_last_error().decode()
+    rc = lib.gdn2_fwd(_lib.F32 | _lib.NO_OUT, *args, 0, 1, 128, 2, 128, 128, 64, 0.1, 1e3, None)
+    assert rc == _lib.ERR_INVALID
+
+
 def test_status_query_rejects_bad_workspace_without_gpu_work():
     lib = _lib.load()
     assert lib.gdn2_workspace_status(None, 1 << 20, None) == _lib.ERR_INVALID
