@@ -168,9 +168,9 @@ def gdn2_segmented_forward_trainable(q, k, v, w, b, g, scale, h0=None, segments=
     this GPU).  Needs BT = D = 128 and T a multiple of segments * BT; falls
     back to the serial path per call whenever a state sanitiser acts."""
     B, T, H, D = q.shape
-    if segments is None:
+    if segments is None:   # planned: only the BT = D = 128 path has the segment joins
         sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-        segments = plan_segments(B, T, H, _fwd.BT, sms)
+        segments = plan_segments(B, T, H, _fwd.BT, sms) if int(_fwd.BT) == 128 and D == 128 else 1
     if h0 is None:
         h0 = torch.zeros((B, H, D, D), dtype=torch.float32, device=q.device)
     if segments <= 1:
