@@ -267,6 +267,16 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     fence_before_sync();
     __syncthreads();   // lo planes and the state in TMEM ready for the MMAs
     fence_after_sync();
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < D / KS; ++s) {
+        const int slot = (it * (D / KS) + s) % kScanSlots;
+        const Opnd B = kmajor(sm + slot * SLICE_FLOATS, lo + s * SLICE_FLOATS, KS);
+        mma3_ta(tmem, tmem + 128 + s * KS, tmem + 256 + s * KS, B, 128, KS / 8, s > 0);
+      }
+      commit(&ts.done);
+    }
+    // the guard test of this step runs while its MMAs do (its bound loads are
+    // off the issue path)
     if (kGuard) {
       float m = ts.wmax[it & 1][0];
 #pragma unroll
@@ -276,14 +286,6 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
       const bool ok = bd[1] + bd[0] * m < p.clip * (1.f - 1e-5f);
       flagged |= !ok;
       if (threadIdx.x == 0) bd[2] = ok ? 0.f : 1.f;
-    }
-    if (threadIdx.x == 0) {
-      for (int s = 0; s < D / KS; ++s) {
-        const int slot = (it * (D / KS) + s) % kScanSlots;
-        const Opnd B = kmajor(sm + slot * SLICE_FLOATS, lo + s * SLICE_FLOATS, KS);
-        mma3_ta(tmem, tmem + 128 + s * KS, tmem + 256 + s * KS, B, 128, KS / 8, s > 0);
-      }
-      commit(&ts.done);
     }
     mbar_wait(&ts.done, ph, ws.status);
     ph ^= 1;
@@ -300,11 +302,12 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     if (PROD) dst = last ? out_final + bh * D * D : nullptr;
     else if (!BWD) dst = last ? (out_final ? out_final + bh * D * D : nullptr) : ws.hpre + (chunk + 1) * D * D;
     else dst = ws.dh + chunk * D * D;
+    float xa[64];   // the thread's 64 accumulator columns, one wait
+    tmem_ld64(lane_quarter_addr(tmem, dcol0), xa);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int c0 = dcol0 + q * 16;
-      float x[16];
-      tmem_ld16(lane_quarter_addr(tmem, c0), x);
+      const float* x = xa + q * 16;
       float hv[16], lv[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
