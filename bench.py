@@ -136,15 +136,23 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.n0 = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.index)],
+                 "-lms", "50", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi prints its first sample as soon as it is up: wait for
+            # it so that the samples cover the region that follows, and keep
+            # only the later ones
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.n0 = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -164,7 +172,7 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        for ln in self.lines:
+        for ln in self.lines[self.n0:] or self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
