@@ -146,19 +146,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_affine(Problem p, Workspace 
 //   backward: dh_c^T    = dh_{c+1}^T M_c + E_c^T (dh_pre of every chunk -> ws.dh)
 // The B operand (M, or M^T backward) arrives from k_tc_affine as four 16 KB
 // canonical K-slices per chunk, streamed by bulk copies through a ring of
-// kScanSlots slots (2.5 chunks ahead).  The raw float32 slice is the hi plane;
-// each step first forms the four lo planes (x - tf32(x)) in shared memory, then
+// kScanSlots slots (1.5 chunks ahead); the constant term (Bc, or E backward)
+// lands in shared memory by one bulk copy a step ahead of its use.  The raw
+// float32 slice is the hi plane; each step first forms the four lo planes (x - tf32(x)) in shared memory, then
 // issues one 128 x 128 x 128 3xTF32 product; the epilogue adds the constant
 // term, sanitises, stores the state and writes it back to TMEM as hi / lo.
 // ---------------------------------------------------------------------------
 // PROD (forward only) instead accumulates the segment map P = M_last ... M_first
 // from P = I with no constant term and no sanitiser, writing only P to
 // out_final (sequence parallelism).
-constexpr int kScanSlots = 10;
+constexpr int kScanSlots = 6;
 constexpr int kScanSliceBytes = SLICE_FLOATS * 4;   // one plane of one slice
 struct ScanSmem {
   float wmax[2][8];   // per-warp max |state|, double-buffered by step parity
   uint64_t full[kScanSlots];
+  uint64_t addfull;    // the step's constant term landed in shared memory
   uint64_t done;
   uint32_t tmem;
 };
@@ -170,12 +172,14 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
   extern __shared__ __align__(128) float sm[];
   __shared__ ScanSmem ts;
   float* lo = sm + kScanSlots * SLICE_FLOATS;
+  float* addt = lo + 4 * SLICE_FLOATS;   // the step's constant term (Bc or E), D x D
   const int h = blockIdx.x, bb = blockIdx.y;
   const size_t bh = (size_t)bb * p.H + h;
   // TMEM: accumulator [0, 128), state hi [128, 256), state lo [256, 384)
   if ((threadIdx.x >> 5) == 0) tmem_alloc(&ts.tmem, 512);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kScanSlots; ++i) mbar_init(&ts.full[i], 1);
+    mbar_init(&ts.addfull, 1);
     mbar_init(&ts.done, 1);
     fence_mbar_init();
   }
@@ -193,8 +197,16 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     mbar_arrive_expect_tx(&ts.full[slot], kScanSliceBytes);
     bulk_g2s(sm + slot * SLICE_FLOATS, src, kScanSliceBytes, &ts.full[slot]);
   };
-  if (threadIdx.x == 0)
+  // the constant term of step `it`, one bulk copy a step ahead of its use
+  auto issue_add = [&](int it) {   // thread 0 only
+    const int c = BWD ? ncs - 1 - it : it;
+    mbar_arrive_expect_tx(&ts.addfull, D * D * 4);
+    bulk_g2s(addt, (BWD ? ws.E : ws.Bc) + (bh * ncs + c) * D * D, D * D * 4, &ts.addfull);
+  };
+  if (threadIdx.x == 0) {
     for (int t = 0; t < kScanSlots && t < nt; ++t) issue(t);
+    if (!PROD) issue_add(0);
+  }
 
   const int warp = threadIdx.x >> 5;
   const int vrow = 32 * (warp & 3) + (threadIdx.x & 31);
@@ -245,9 +257,9 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
     const int c = BWD ? ncs - 1 - it : it;
     const size_t chunk = bh * ncs + c;
     if (!PROD) {   // this thread's share of the constant term (row v, 64 columns d)
-      const float* add = (BWD ? ws.E : ws.Bc) + chunk * D * D;
+      mbar_wait(&ts.addfull, (uint32_t)(it & 1), ws.status);
 #pragma unroll
-      for (int j = 0; j < 64; ++j) addv[j] = add[(dcol0 + j) * D + vrow];
+      for (int j = 0; j < 64; ++j) addv[j] = addt[(dcol0 + j) * D + vrow];
     }
     // lo planes of this step's four slices
 #pragma unroll 1
@@ -274,6 +286,12 @@ k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __rest
         mma3_ta(tmem, tmem + 128 + s * KS, tmem + 256 + s * KS, B, 128, KS / 8, s > 0);
       }
       commit(&ts.done);
+      // every thread read its constant term before the barrier above: the
+      // next step's tile may land
+      if (!PROD && it + 1 < ncs) {
+        fence_async_smem();
+        issue_add(it + 1);
+      }
     }
     // the guard test of this step runs while its MMAs do (its bound loads are
     // off the issue path)
@@ -525,7 +543,7 @@ cudaError_t prep(K kern, size_t smem) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 constexpr size_t kRing3 = 2 * 3 * (size_t)SLICE_BYTES;   // 192 KB
-constexpr size_t kScan = (kScanSlots + 4) * (size_t)kScanSliceBytes;   // raw ring + lo, 224 KB
+constexpr size_t kScan = (kScanSlots + 8) * (size_t)kScanSliceBytes;   // raw ring + lo + constant term, 224 KB
 }  // namespace
 
 cudaError_t launch_tc_fwd(const Problem& p, const Workspace& ws, const float* h0, float* o,
