@@ -61,3 +61,24 @@ def test_bench_tables_cover_every_profiled_stage():
     assert bench._shard(bench.CONFIGS[1], 8, 0, "strong") == (1, 6)
     assert bench._shard(bench.CONFIGS[1], 4, 0, "strong") == (2, 6)
     assert bench._shard(bench.CONFIGS[1], 8, 0, "weak") == (8, 6)
+
+
+def test_clock_summary_reads_only_samples_after_startup():
+    """The bench's clock record: median SM clock and the throttle reasons seen
+    in the samples taken after nvidia-smi's first (start-up) line."""
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    clk = bench.ClockSampler(0)
+    row = "0, {sm}, 1965, 700.0, 0x0, Not Active, Not Active, {thermal}, {cap}"
+    clk.lines = [row.format(sm=345, thermal="Not Active", cap="Not Active"),   # idle, before the region
+                 row.format(sm=1965, thermal="Not Active", cap="Not Active"),
+                 row.format(sm=1965, thermal="Not Active", cap="Active"),
+                 row.format(sm=1950, thermal="Active", cap="Not Active"),
+                 "garbled"]
+    clk.n0 = 1
+    s = clk.summary()
+    assert s["samples"] == 3 and s["sm_mhz"] == 1965 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
+    clk.n0 = len(clk.lines)   # no sample after start-up: fall back to every line
+    assert clk.summary()["samples"] == 4
