@@ -168,7 +168,8 @@ struct ScanSmem {
 template <bool BWD, bool PROD = false>
 __global__ void __launch_bounds__(kThreads, 1)
 k_tc_scan(Problem p, Workspace ws, const float* __restrict__ init, float* __restrict__ out_final) {
-  // shared memory: kScanSlots raw slices, then the 4 lo planes of the step
+  // shared memory: kScanSlots raw slices, the 4 lo planes of the step, the
+  // step's constant term
   extern __shared__ __align__(128) float sm[];
   __shared__ ScanSmem ts;
   float* lo = sm + kScanSlots * SLICE_FLOATS;
